@@ -1,0 +1,222 @@
+// C ABI of libfa_b200.so (declared in include/fa_b200.h): argument validation, tensor-map
+// encoding, the per-device watchdog word and the head-sharding launcher.
+//
+// Validation mirrors the reference's fa::flash_fwd (csrc/kernels/flash_fwd.cu:625-652):
+// same conditions, same messages, reported through return codes + fa_last_error() because a C
+// ABI cannot throw.
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "../../include/fa_b200.h"
+#include "fa_internal.h"
+#include "tma_host.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+int cuda_fail(cudaError_t err, const char* what) {
+    return fail(FA_ERR_CUDA, std::string("flash_fwd: CUDA error in ") + what + ": " +
+                                 cudaGetErrorString(err));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// One watchdog record per device, a file-scope __device__ variable; its address on each device
+// is looked up once (with that device current) and cached.
+__device__ fa_sm100::DeviceStatus g_device_status;
+
+constexpr int kMaxDevices = 64;
+std::mutex g_status_mutex;
+fa_sm100::DeviceStatus* g_status_ptr[kMaxDevices] = {};
+std::atomic<unsigned> g_epoch{0};
+
+cudaError_t status_ptr_for(int device, fa_sm100::DeviceStatus** out) {
+    if (device < 0 || device >= kMaxDevices) {
+        return cudaErrorInvalidDevice;
+    }
+    std::lock_guard<std::mutex> lock(g_status_mutex);
+    if (g_status_ptr[device] == nullptr) {
+        void* p = nullptr;
+        const cudaError_t err = cudaGetSymbolAddress(&p, g_device_status);
+        if (err != cudaSuccess) {
+            return err;
+        }
+        g_status_ptr[device] = static_cast<fa_sm100::DeviceStatus*>(p);
+    }
+    *out = g_status_ptr[device];
+    return cudaSuccess;
+}
+
+unsigned next_epoch() {
+    unsigned e = g_epoch.fetch_add(1, std::memory_order_relaxed) + 1;
+    if (e == 0) {
+        e = g_epoch.fetch_add(1, std::memory_order_relaxed) + 1;
+    }
+    return e;
+}
+
+int validate(const FaFwdParams* p) {
+    if (p == nullptr) {
+        return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd: params is NULL");
+    }
+    if (p->batch <= 0 || p->heads <= 0 || p->seqlen <= 0) {
+        return fail(FA_ERR_INVALID_ARGUMENT,
+                    "flash_fwd: batch, heads and seqlen must be positive");
+    }
+    if (static_cast<int64_t>(p->batch) * p->heads > 65535) {
+        return fail(FA_ERR_INVALID_ARGUMENT,
+                    "flash_fwd: batch * heads must be <= 65535 (grid.y limit)");
+    }
+    if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v) || !aligned16(p->o)) {
+        return fail(FA_ERR_INVALID_ARGUMENT,
+                    "flash_fwd: tensors must be 16-byte aligned (TMA)");
+    }
+    if (p->head_dim != 64 && p->head_dim != 128) {
+        return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd: head_dim must be 64 or 128, got " +
+                                                 std::to_string(p->head_dim));
+    }
+    if (p->variant > FA_VARIANT_FP16ACC) {
+        return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd: unknown variant");
+    }
+    if (p->q == nullptr || p->k == nullptr || p->v == nullptr || p->o == nullptr) {
+        return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd: null tensor pointer");
+    }
+    return FA_OK;
+}
+
+int launch_one(const FaFwdParams* p, cudaStream_t stream) {
+    const int rc = validate(p);
+    if (rc != FA_OK) {
+        return rc;
+    }
+    int device = 0;
+    cudaError_t err = cudaGetDevice(&device);
+    if (err != cudaSuccess) {
+        return cuda_fail(err, "cudaGetDevice");
+    }
+    fa_sm100::DeviceStatus* status = nullptr;
+    err = status_ptr_for(device, &status);
+    if (err != cudaSuccess) {
+        return cuda_fail(err, "cudaGetSymbolAddress");
+    }
+    const int bh = p->batch * p->heads;
+    CUtensorMap maps[4];
+    const void* ptrs[4] = {p->q, p->k, p->v, p->o};
+    for (int i = 0; i < 4; ++i) {
+        const CUresult cr =
+            fa_sm100::encode_bhnd_map(&maps[i], ptrs[i], bh, p->seqlen, p->head_dim, 128);
+        if (cr != CUDA_SUCCESS) {
+            return fail(FA_ERR_CUDA, "flash_fwd: cuTensorMapEncodeTiled failed (CUresult " +
+                                         std::to_string(static_cast<int>(cr)) + ")");
+        }
+    }
+    fa_sm100::FwdArgs args{};
+    args.seqlen = p->seqlen;
+    args.num_bh = bh;
+    args.scale_log2 = static_cast<float>(static_cast<double>(p->softmax_scale) * M_LOG2E);
+    args.epoch = next_epoch();
+    args.status = status;
+    err = fa_sm100::launch_forward(p->head_dim, p->causal != 0, p->variant, maps[0], maps[1],
+                                   maps[2], maps[3], args, stream);
+    if (err != cudaSuccess) {
+        return cuda_fail(err, "kernel launch");
+    }
+    g_last_error.clear();
+    return FA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fa_flash_fwd(const FaFwdParams* params, fa_stream_t stream) {
+    return launch_one(params, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fa_flash_fwd_sharded(const FaFwdParams* shards, const int32_t* devices,
+                         const fa_stream_t* streams, int32_t num_shards) {
+    if (num_shards < 0 || (num_shards > 0 && (shards == nullptr || devices == nullptr))) {
+        return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd_sharded: bad shard list");
+    }
+    int prev = 0;
+    cudaError_t err = cudaGetDevice(&prev);
+    if (err != cudaSuccess) {
+        return cuda_fail(err, "cudaGetDevice");
+    }
+    int rc = FA_OK;
+    for (int i = 0; i < num_shards && rc == FA_OK; ++i) {
+        err = cudaSetDevice(devices[i]);
+        if (err != cudaSuccess) {
+            rc = cuda_fail(err, "cudaSetDevice");
+            break;
+        }
+        rc = launch_one(&shards[i],
+                        streams != nullptr ? reinterpret_cast<cudaStream_t>(streams[i]) : nullptr);
+    }
+    cudaSetDevice(prev);
+    return rc;
+}
+
+const char* fa_last_error(void) { return g_last_error.c_str(); }
+
+int fa_device_status(int32_t device, int32_t clear, uint32_t* status_out) {
+    int prev = 0;
+    cudaError_t err = cudaGetDevice(&prev);
+    if (err != cudaSuccess) {
+        return cuda_fail(err, "cudaGetDevice");
+    }
+    err = cudaSetDevice(device);
+    if (err != cudaSuccess) {
+        return cuda_fail(err, "cudaSetDevice");
+    }
+    fa_sm100::DeviceStatus* ptr = nullptr;
+    fa_sm100::DeviceStatus host{};
+    err = status_ptr_for(device, &ptr);
+    if (err == cudaSuccess) {
+        err = cudaDeviceSynchronize();
+    }
+    if (err == cudaSuccess) {
+        err = cudaMemcpy(&host, ptr, sizeof(host), cudaMemcpyDeviceToHost);
+    }
+    if (err == cudaSuccess && clear != 0) {
+        const fa_sm100::DeviceStatus zero{};
+        err = cudaMemcpy(ptr, &zero, sizeof(zero), cudaMemcpyHostToDevice);
+    }
+    cudaSetDevice(prev);
+    if (err != cudaSuccess) {
+        return cuda_fail(err, "fa_device_status");
+    }
+    if (status_out != nullptr) {
+        *status_out = host.code;
+    }
+    return FA_OK;
+}
+
+int fa_kernel_info(int32_t head_dim, int32_t variant, int32_t* smem_bytes, int32_t* threads) {
+    if ((head_dim != 64 && head_dim != 128) || variant < 0 || variant > FA_VARIANT_FP16ACC) {
+        return fail(FA_ERR_INVALID_ARGUMENT, "fa_kernel_info: bad head_dim or variant");
+    }
+    if (smem_bytes != nullptr) {
+        *smem_bytes = fa_sm100::kernel_smem_bytes(head_dim, false, variant);
+    }
+    if (threads != nullptr) {
+        *threads = fa_sm100::kernel_threads(head_dim, false, variant);
+    }
+    return FA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,687 @@
+// FlashAttention-2 forward for B200 (sm_100a): TMA + mbarrier ring, tcgen05.mma into tensor
+// memory, online base-2 softmax in warpgroups that own one TMEM lane (= one query row) per
+// thread, TMA epilogue.
+//
+//   O = softmax(Q K^T * scale) V        Q, K, V, O: [B, H, N, D] fp16, D in {64, 128}
+//
+// It replaces the reference's mma.sync kernel (csrc/kernels/flash_fwd.cu:154-561) and its
+// launcher (:563-652) behind the same parameters; the algorithm (FA2 online softmax with the
+// scale folded into a base-2 exponent, causal tiles above the diagonal skipped, masking only
+// on diagonal / ragged tiles, lazy rescaling for the "opt" variant, per-tile fp16 partials for
+// "fp16acc") is the reference's, the machine mapping is new:
+//
+// CTA = one (b,h) head x NQ consecutive 128-row query tiles (NQ = 2, or 1 for fp16acc).
+// Warp roles (warp-specialised, one CTA per SM):
+//   warps 0 .. 4*NQ-1   softmax warpgroup t = warp/4 owns query tile t; thread i of the
+//                       warpgroup owns TMEM lane i = query row i of the tile. Row max and
+//                       row sum need no shuffles. It also rescales O in TMEM when its running
+//                       max moves, and runs the epilogue of its tile.
+//   warp 4*NQ           TMA producer: Q tiles once, then K_0, V_0, K_1, V_1, ... through a
+//                       STAGES-deep ring of 128 x D tiles in 128-byte-swizzled shared memory.
+//   warp 4*NQ+1         MMA issuer (one thread): S_t = Q_t K_j^T (SS MMA, M=128 N=128) into
+//                       TMEM; O_t += P_t V_j (TS MMA: P from TMEM, V from smem, N = D).
+//
+// Tensor memory (512 columns x 128 lanes, fp32 cells):
+//   S_t  columns [128 t, 128 t + 128)        scores of tile t, fp32
+//   P_t  columns [128 t, 128 t + 64)         probabilities, fp16 packed 2 per column,
+//                                            written over S_t once S_t has been read
+//   O_t  columns [128 NQ + D t, ... + D)     fp32 output accumulator of tile t
+//   T_h  columns [128 NQ + D NQ + D h, ...)  fp16acc only: fp16 partial of P.V over keys
+//                                            [64 h, 64 h + 64) of the current K/V tile
+//
+// The MMA issuer orders, per key tile j:  PV_0(j), S_0(j+1), PV_1(j), S_1(j+1). S_t(j+1) is
+// issued after PV_t(j), which reads P_t(j) from the same columns (tcgen05.mma operations of
+// one thread execute in issue order).
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "fa_internal.h"
+#include "sm100_ptx.cuh"
+
+namespace fa_sm100 {
+
+constexpr int kBM = 128;             // query rows per tile (= TMEM lanes = MMA M)
+constexpr int kBN = 128;             // keys per K/V tile (= MMA N of Q K^T)
+constexpr int kBoxBytes = 128 * 128; // one TMA box: 128 rows x 64 fp16 (128 B, one swizzle span)
+
+template <int D_, bool CAUSAL_, int VARIANT_>
+struct FwdCfg {
+    static constexpr int D = D_;
+    static constexpr bool CAUSAL = CAUSAL_;
+    static constexpr int VARIANT = VARIANT_;
+    // fp16acc: P.V accumulated in fp16 per 64 keys, folded into fp32 (reference ACC16), with
+    // two fp16 exponentials per instruction (reference EXP16). Exact max (no lazy rescale).
+    static constexpr bool ACC16 = (VARIANT_ == kVariantFp16Acc);
+    static constexpr bool EXP16 = ACC16;
+    // Lazy rescale (reference LAZY, flash_fwd.cu:365-376): keep a stale row max until the
+    // tile max exceeds it by more than 2^8. Threshold 0 = exact running max.
+    static constexpr float kRescaleThreshold = (VARIANT_ == kVariantOpt) ? 8.0f : 0.0f;
+    static constexpr int NQ = ACC16 ? 1 : 2;
+    static constexpr int kTileBytes = kBM * D * 2;  // one Q, K, V or O tile (BM == BN)
+    static constexpr int kBoxes = D / 64;           // TMA boxes per tile
+    static constexpr int STAGES = (D == 128) ? 4 : 8;
+    // Shared memory (offsets from a 1024-byte aligned base).
+    static constexpr int kSmemQ = 0;
+    static constexpr int kSmemKV = NQ * kTileBytes;
+    static constexpr int kSmemBytes = kSmemKV + STAGES * kTileBytes;
+    static constexpr int kSmemAlloc = kSmemBytes + 1024;
+    // Tensor memory columns.
+    static constexpr int kTmemS = 0;
+    static constexpr int kTmemO = NQ * kBN;
+    static constexpr int kTmemT = kTmemO + NQ * D;
+    static constexpr int kTmemUsed = kTmemT + (ACC16 ? 2 * D : 0);
+    static constexpr int kTmemCols = 512;
+    static_assert(kTmemUsed <= kTmemCols, "tensor memory budget");
+    // Warps.
+    static constexpr int kSoftmaxWarps = 4 * NQ;
+    static constexpr int kProducerWarp = kSoftmaxWarps;
+    static constexpr int kMmaWarp = kSoftmaxWarps + 1;
+    static constexpr int kThreads = 32 * (kSoftmaxWarps + 2);
+    static_assert(D == 64 || D == 128, "head dim");
+    static_assert(kSmemAlloc <= 227 * 1024, "shared memory budget");
+    static_assert(kSmemAlloc > 114 * 1024, "one CTA per SM (it owns all 512 TMEM columns)");
+};
+
+struct SharedBarriers {
+    uint64_t q_full[2];
+    uint64_t kv_full[8];
+    uint64_t kv_empty[8];
+    uint64_t s_full[2];
+    uint64_t p_full[2];
+    uint64_t o_done[2];
+    uint64_t epi[2];
+    uint64_t mma_idle;
+    uint32_t tmem_base;
+    int abort;
+};
+
+__device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
+__device__ __forceinline__ uint32_t f2u(float x) { return __float_as_uint(x); }
+
+// fp16 accumulator cells hold one value per 32-bit column, in the low half.
+__device__ __forceinline__ float f16cell_to_float(uint32_t cell) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(cell & 0xFFFFu)));
+}
+
+template <class Cfg>
+__device__ __forceinline__ void issue_s_mma(uint32_t tmem_s, uint32_t q_addr, uint32_t k_addr) {
+    constexpr uint32_t idesc = make_idesc_f16(kBM, kBN, /*d_f32=*/true, /*b_mn_major=*/false);
+#pragma unroll
+    for (int kk = 0; kk < Cfg::D / 16; ++kk) {
+        const uint32_t off = static_cast<uint32_t>((kk / 4) * kBoxBytes + (kk % 4) * 32);
+        umma_ss(tmem_s, make_desc_kmajor_sw128(q_addr + off), make_desc_kmajor_sw128(k_addr + off),
+                idesc, kk > 0 ? 1u : 0u);
+    }
+}
+
+// O (fp32) += P V over the 128 keys of one tile; `first` starts the accumulator.
+template <class Cfg>
+__device__ __forceinline__ void issue_pv_mma_f32(uint32_t tmem_o, uint32_t tmem_p, uint32_t v_addr,
+                                                 bool first) {
+    constexpr uint32_t idesc = make_idesc_f16(kBM, Cfg::D, /*d_f32=*/true, /*b_mn_major=*/true);
+#pragma unroll
+    for (int kk = 0; kk < kBN / 16; ++kk) {
+        umma_ts(tmem_o, tmem_p + kk * 8, make_desc_mnmajor_sw128(v_addr + kk * 2048, kBoxBytes),
+                idesc, (first && kk == 0) ? 0u : 1u);
+    }
+}
+
+// fp16acc: T_h = P[:, 64h:64h+64] V[64h:64h+64, :] accumulated in fp16, fresh per tile.
+template <class Cfg>
+__device__ __forceinline__ void issue_pv_mma_f16(uint32_t tmem_t, uint32_t tmem_p, uint32_t v_addr) {
+    constexpr uint32_t idesc = make_idesc_f16(kBM, Cfg::D, /*d_f32=*/false, /*b_mn_major=*/true);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+        for (int k4 = 0; k4 < 4; ++k4) {
+            const int kk = h * 4 + k4;
+            umma_ts(tmem_t + h * Cfg::D, tmem_p + kk * 8,
+                    make_desc_mnmajor_sw128(v_addr + kk * 2048, kBoxBytes), idesc,
+                    k4 == 0 ? 0u : 1u);
+        }
+    }
+}
+
+template <class Cfg>
+__global__ void __launch_bounds__(Cfg::kThreads, 1)
+    fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
+                        const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v,
+                        const __grid_constant__ CUtensorMap tm_o, const FwdArgs args) {
+    constexpr int D = Cfg::D;
+    constexpr int NQ = Cfg::NQ;
+    constexpr int STAGES = Cfg::STAGES;
+
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ SharedBarriers sb;
+
+    const int warp = static_cast<int>(threadIdx.x) / 32;
+    const int lane = static_cast<int>(threadIdx.x) % 32;
+
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const uint32_t smem_base = smem_u32(smem);
+
+    const int n = args.seqlen;
+    const int bh = static_cast<int>(blockIdx.y);
+    // Causal: block x covers more key tiles the later its rows are; launch the longest first.
+    const int m_block = Cfg::CAUSAL ? static_cast<int>(gridDim.x - 1 - blockIdx.x)
+                                    : static_cast<int>(blockIdx.x);
+    const int q_row0 = m_block * NQ * kBM;
+    const int n_tiles_all = (n + kBN - 1) / kBN;
+    int n_kv[NQ];
+    int n_max = 0;
+#pragma unroll
+    for (int t = 0; t < NQ; ++t) {
+        const int q0 = q_row0 + t * kBM;
+        n_kv[t] = (q0 >= n) ? 0 : (Cfg::CAUSAL ? (q0 / kBN + 1) : n_tiles_all);
+        n_max = max(n_max, n_kv[t]);
+    }
+
+    const WaitCtx wctx{&sb.abort, &args.status->code, &args.status->epoch_aborted, args.epoch};
+
+    if (threadIdx.x == 0) {
+        sb.abort = 0;
+        for (int t = 0; t < NQ; ++t) {
+            mbar_init(smem_u32(&sb.q_full[t]), 1);
+            mbar_init(smem_u32(&sb.s_full[t]), 1);
+            mbar_init(smem_u32(&sb.p_full[t]), 128);
+            mbar_init(smem_u32(&sb.o_done[t]), 1);
+            mbar_init(smem_u32(&sb.epi[t]), 128);
+        }
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(&sb.kv_full[s]), 1);
+            mbar_init(smem_u32(&sb.kv_empty[s]), 1);
+        }
+        mbar_init(smem_u32(&sb.mma_idle), 1);
+        mbar_fence_init();
+    }
+    if (warp == Cfg::kMmaWarp) {
+        tmem_alloc(smem_u32(&sb.tmem_base), Cfg::kTmemCols);
+        tmem_relinquish();
+    }
+    if (warp == Cfg::kProducerWarp && lane == 0) {
+        tma_prefetch_desc(&tm_q);
+        tma_prefetch_desc(&tm_k);
+        tma_prefetch_desc(&tm_v);
+        tma_prefetch_desc(&tm_o);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = sb.tmem_base;
+
+    if (warp < Cfg::kSoftmaxWarps) {
+        // ================================ softmax warpgroups ================================
+        const int t = warp / 4;
+        const int row = (warp % 4) * 32 + lane;  // TMEM lane == query row within the tile
+        const int q0 = q_row0 + t * kBM;
+        const int grow = q0 + row;                // global query row
+        const uint32_t lane_off = static_cast<uint32_t>((warp % 4) * 32) << 16;
+        const uint32_t t_s = tmem + lane_off + Cfg::kTmemS + t * kBN;
+        const uint32_t t_o = tmem + lane_off + Cfg::kTmemO + t * D;
+        const uint32_t t_t = tmem + lane_off + Cfg::kTmemT;
+        const uint32_t bar_s = smem_u32(&sb.s_full[t]);
+        const uint32_t bar_p = smem_u32(&sb.p_full[t]);
+        const uint32_t bar_o = smem_u32(&sb.o_done[t]);
+        const float scale_log2 = args.scale_log2;
+        const int nt = n_kv[t];
+        // Last key index this row may see: keys > lim are masked (ragged N, causal).
+        const int lim = Cfg::CAUSAL ? min(n - 1, grow) : (n - 1);
+
+        float row_max = -INFINITY;  // running max of the scaled scores (log2 units)
+        float row_sum = 0.0f;       // running sum of the fp16-rounded probabilities
+        bool ok = true;
+
+        for (int j = 0; j < nt; ++j) {
+            ok = __all_sync(0xffffffffu, mbar_wait(bar_s, j & 1, wctx, kStatusTimeoutSoftmax));
+            if (!ok) {
+                break;
+            }
+            tc_fence_after();
+            uint32_t sr[kBN];
+#pragma unroll
+            for (int c = 0; c < kBN / 32; ++c) {
+                tmem_ld32(t_s + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+            }
+            tmem_wait_ld();
+
+            const int kbase = j * kBN;
+            // Only the last tile can hold keys >= N, and for causal rows only the last tile
+            // (the diagonal one) holds keys after the row: every other tile is unmasked.
+            const bool masked = (kbase + kBN > n) || (Cfg::CAUSAL && j == nt - 1);
+            float tile_max;
+            float mul;
+            if (masked) {
+                // Diagonal / ragged tile: scale first, then mask, so masked scores are -inf
+                // whatever the sign of the scale.
+                const int cmax = lim - kbase;
+                float mx[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    mx[i] = -INFINITY;
+                }
+#pragma unroll
+                for (int c = 0; c < kBN; ++c) {
+                    const float x = (c > cmax) ? -INFINITY : u2f(sr[c]) * scale_log2;
+                    sr[c] = f2u(x);
+                    mx[c % 8] = fmaxf(mx[c % 8], x);
+                }
+                tile_max = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+                mul = 1.0f;
+            } else {
+                float mx[8];
+                if (scale_log2 >= 0.0f) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        mx[i] = u2f(sr[i]);
+                    }
+#pragma unroll
+                    for (int c = 8; c < kBN; ++c) {
+                        mx[c % 8] = fmaxf(mx[c % 8], u2f(sr[c]));
+                    }
+                    tile_max = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                     fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        mx[i] = u2f(sr[i]);
+                    }
+#pragma unroll
+                    for (int c = 8; c < kBN; ++c) {
+                        mx[c % 8] = fminf(mx[c % 8], u2f(sr[c]));
+                    }
+                    tile_max = fminf(fminf(fminf(mx[0], mx[1]), fminf(mx[2], mx[3])),
+                                     fminf(fminf(mx[4], mx[5]), fminf(mx[6], mx[7])));
+                }
+                tile_max *= scale_log2;
+                mul = scale_log2;
+            }
+
+            // Running max update (lazy for "opt": keep the old max unless it grew by > 2^8).
+            const float new_max = (tile_max > row_max + Cfg::kRescaleThreshold) ? tile_max : row_max;
+            const float max_used = (new_max == -INFINITY) ? 0.0f : new_max;
+            const bool grew = (new_max != row_max);
+            const float alpha = grew ? ex2_approx(row_max - max_used) : 1.0f;  // 0 on tile 0
+            row_max = new_max;
+            const float neg_max = -max_used;
+
+            // Probabilities, packed fp16 pairs, into the S columns (P_t).
+            float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                uint32_t pk[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int c = half * 64 + 2 * i;
+                    const float x0 = fmaf(u2f(sr[c]), mul, neg_max);
+                    const float x1 = fmaf(u2f(sr[c + 1]), mul, neg_max);
+                    uint32_t h;
+                    if constexpr (Cfg::EXP16) {
+                        h = ex2_approx_f16x2(pack_half2(x0, x1));
+                    } else {
+                        h = pack_half2(ex2_approx(x0), ex2_approx(x1));
+                    }
+                    const float2 pf = unpack_half2(h);
+                    part[i % 4] += pf.x + pf.y;
+                    pk[i] = h;
+                }
+                tmem_st32(t_s + half * 32, pk);
+            }
+            row_sum = row_sum * alpha + ((part[0] + part[1]) + (part[2] + part[3]));
+
+            if constexpr (!Cfg::ACC16) {
+                // Rescale O when some row of this warp moved its max (rare with the lazy rule).
+                // O holds P.V up to tile j-1: wait for that MMA first.
+                if (j > 0 && __any_sync(0xffffffffu, grew)) {
+                    ok = __all_sync(0xffffffffu,
+                                    mbar_wait(bar_o, (j - 1) & 1, wctx, kStatusTimeoutSoftmax));
+                    if (!ok) {
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int c = 0; c < D / 32; ++c) {
+                        uint32_t o[32];
+                        tmem_ld32(t_o + c * 32, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) {
+                            o[e] = f2u(u2f(o[e]) * alpha);
+                        }
+                        tmem_st32(t_o + c * 32, o);
+                    }
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(bar_p);
+            } else {
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(bar_p);
+                // Fold this tile's two fp16 partials into the fp32 accumulator:
+                // O = alpha * O + T_0 + T_1.
+                ok = __all_sync(0xffffffffu, mbar_wait(bar_o, j & 1, wctx, kStatusTimeoutSoftmax));
+                if (!ok) {
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < D / 32; ++c) {
+                    uint32_t a[32];
+                    uint32_t b[32];
+                    uint32_t o[32];
+                    tmem_ld32(t_t + c * 32, a);
+                    tmem_ld32(t_t + D + c * 32, b);
+                    if (j > 0) {
+                        tmem_ld32(t_o + c * 32, o);
+                    }
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        const float v = f16cell_to_float(a[e]) + f16cell_to_float(b[e]);
+                        o[e] = f2u(j > 0 ? fmaf(u2f(o[e]), alpha, v) : v);
+                    }
+                    tmem_st32(t_o + c * 32, o);
+                }
+                tmem_wait_st();
+            }
+        }
+
+        // ----------------------------------- epilogue -----------------------------------
+        if (ok && nt > 0) {
+            if constexpr (!Cfg::ACC16) {
+                ok = __all_sync(0xffffffffu,
+                                mbar_wait(bar_o, (nt - 1) & 1, wctx, kStatusTimeoutSoftmax));
+                tc_fence_after();
+            }
+        }
+        if (ok && nt > 0) {
+            const float inv_sum = (row_sum > 0.0f) ? (1.0f / row_sum) : 0.0f;
+            // Stage O (fp16) in this tile's Q buffer, in the swizzled layout of the TMA box.
+            // Every MMA that read Q_t has completed (its S was consumed above).
+            uint8_t* out = smem + Cfg::kSmemQ + t * Cfg::kTileBytes;
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+                uint32_t o[32];
+                tmem_ld32(t_o + c * 32, o);
+                tmem_wait_ld();
+                uint32_t h[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    h[e] = pack_half2(u2f(o[2 * e]) * inv_sum, u2f(o[2 * e + 1]) * inv_sum);
+                }
+                const int box = (c * 32) / 64;
+                const int chunk0 = ((c * 32) % 64) / 8;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int cc = chunk0 + i;
+                    uint4* dst = reinterpret_cast<uint4*>(out + box * kBoxBytes + row * 128 +
+                                                          ((cc ^ (row & 7)) << 4));
+                    *dst = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+                }
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(smem_u32(&sb.epi[t]));
+            if (row == 0) {
+                if (mbar_wait(smem_u32(&sb.epi[t]), 0, wctx, kStatusTimeoutEpilogue)) {
+#pragma unroll
+                    for (int b = 0; b < Cfg::kBoxes; ++b) {
+                        tma_store_3d(&tm_o, smem_u32(out) + b * kBoxBytes, b * 64, q0, bh);
+                    }
+                    tma_store_commit();
+                    tma_store_wait_read();
+                }
+            }
+            __syncwarp();
+        }
+    } else if (warp == Cfg::kProducerWarp) {
+        // ================================== TMA producer ===================================
+        if (lane == 0) {
+            int last_parity[STAGES];
+            bool loaded[STAGES];
+#pragma unroll
+            for (int s = 0; s < STAGES; ++s) {
+                loaded[s] = false;
+                last_parity[s] = 0;
+            }
+            bool ok = true;
+#pragma unroll
+            for (int t = 0; t < NQ; ++t) {
+                if (n_kv[t] > 0) {
+                    const uint32_t bar = smem_u32(&sb.q_full[t]);
+                    mbar_arrive_expect_tx(bar, Cfg::kTileBytes);
+#pragma unroll
+                    for (int b = 0; b < Cfg::kBoxes; ++b) {
+                        tma_load_3d(smem_base + Cfg::kSmemQ + t * Cfg::kTileBytes + b * kBoxBytes,
+                                    &tm_q, bar, b * 64, q_row0 + t * kBM, bh);
+                    }
+                }
+            }
+            int ring = 0;
+            for (int j = 0; j < n_max && ok; ++j) {
+#pragma unroll
+                for (int kind = 0; kind < 2; ++kind) {
+                    const int stage = ring % STAGES;
+                    const int phase = (ring / STAGES) & 1;
+                    if (!mbar_wait(smem_u32(&sb.kv_empty[stage]), phase ^ 1, wctx,
+                                   kStatusTimeoutProducer)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t bar = smem_u32(&sb.kv_full[stage]);
+                    mbar_arrive_expect_tx(bar, Cfg::kTileBytes);
+                    const CUtensorMap* map = (kind == 0) ? &tm_k : &tm_v;
+#pragma unroll
+                    for (int b = 0; b < Cfg::kBoxes; ++b) {
+                        tma_load_3d(smem_base + Cfg::kSmemKV + stage * Cfg::kTileBytes + b * kBoxBytes,
+                                    map, bar, b * 64, j * kBN, bh);
+                    }
+                    loaded[stage] = true;
+                    last_parity[stage] = phase;
+                    ++ring;
+                }
+            }
+            if (!ok) {
+                // Let every copy still in flight land before the CTA releases its memory.
+                for (int s = 0; s < STAGES; ++s) {
+                    if (loaded[s]) {
+                        mbar_wait_drain(smem_u32(&sb.kv_full[s]), last_parity[s], wctx,
+                                        kStatusTimeoutTeardown);
+                    }
+                }
+                for (int t = 0; t < NQ; ++t) {
+                    if (n_kv[t] > 0) {
+                        mbar_wait_drain(smem_u32(&sb.q_full[t]), 0, wctx, kStatusTimeoutTeardown);
+                    }
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+        // ================================== MMA issuer ====================================
+        if (lane == 0) {
+            bool ok = true;
+#pragma unroll
+            for (int t = 0; t < NQ; ++t) {
+                if (ok && n_kv[t] > 0) {
+                    ok = mbar_wait(smem_u32(&sb.q_full[t]), 0, wctx, kStatusTimeoutMma);
+                }
+            }
+            const uint32_t q_addr0 = smem_base + Cfg::kSmemQ;
+            const uint32_t kv_addr0 = smem_base + Cfg::kSmemKV;
+            int ring = 0;
+            if (ok && n_max > 0) {
+                ok = mbar_wait(smem_u32(&sb.kv_full[0]), 0, wctx, kStatusTimeoutMma);
+                if (ok) {
+                    tc_fence_after();
+#pragma unroll
+                    for (int t = 0; t < NQ; ++t) {
+                        if (n_kv[t] > 0) {
+                            issue_s_mma<Cfg>(tmem + Cfg::kTmemS + t * kBN,
+                                             q_addr0 + t * Cfg::kTileBytes, kv_addr0);
+                            umma_commit(smem_u32(&sb.s_full[t]));
+                        }
+                    }
+                    umma_commit(smem_u32(&sb.kv_empty[0]));
+                    ring = 1;
+                }
+            }
+            for (int j = 0; ok && j < n_max; ++j) {
+                const int v_slot = ring++;
+                const int vs = v_slot % STAGES;
+                ok = mbar_wait(smem_u32(&sb.kv_full[vs]), (v_slot / STAGES) & 1, wctx,
+                               kStatusTimeoutMma);
+                if (!ok) {
+                    break;
+                }
+                tc_fence_after();
+                const bool has_next = (j + 1 < n_max);
+                const int k_slot = has_next ? ring++ : 0;
+                const int ks = k_slot % STAGES;
+                bool k_ready = false;
+#pragma unroll
+                for (int t = 0; t < NQ; ++t) {
+                    if (!ok || j >= n_kv[t]) {
+                        continue;
+                    }
+                    ok = mbar_wait(smem_u32(&sb.p_full[t]), j & 1, wctx, kStatusTimeoutMma);
+                    if (!ok) {
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t tmem_p = tmem + Cfg::kTmemS + t * kBN;
+                    const uint32_t v_addr = kv_addr0 + vs * Cfg::kTileBytes;
+                    if constexpr (Cfg::ACC16) {
+                        issue_pv_mma_f16<Cfg>(tmem + Cfg::kTmemT, tmem_p, v_addr);
+                    } else {
+                        issue_pv_mma_f32<Cfg>(tmem + Cfg::kTmemO + t * Cfg::D, tmem_p, v_addr,
+                                              j == 0);
+                    }
+                    umma_commit(smem_u32(&sb.o_done[t]));
+                    if (j + 1 < n_kv[t]) {
+                        if (!k_ready) {
+                            ok = mbar_wait(smem_u32(&sb.kv_full[ks]), (k_slot / STAGES) & 1, wctx,
+                                           kStatusTimeoutMma);
+                            if (!ok) {
+                                break;
+                            }
+                            tc_fence_after();
+                            k_ready = true;
+                        }
+                        issue_s_mma<Cfg>(tmem + Cfg::kTmemS + t * kBN,
+                                         q_addr0 + t * Cfg::kTileBytes,
+                                         kv_addr0 + ks * Cfg::kTileBytes);
+                        umma_commit(smem_u32(&sb.s_full[t]));
+                    }
+                }
+                if (!ok) {
+                    break;
+                }
+                umma_commit(smem_u32(&sb.kv_empty[vs]));
+                if (has_next) {
+                    umma_commit(smem_u32(&sb.kv_empty[ks]));
+                }
+            }
+            // Every MMA issued above must be complete before tensor memory is released.
+            umma_commit(smem_u32(&sb.mma_idle));
+            mbar_wait_drain(smem_u32(&sb.mma_idle), 0, wctx, kStatusTimeoutTeardown);
+        }
+        __syncwarp();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == Cfg::kMmaWarp) {
+        tc_fence_after();
+        tmem_dealloc(tmem, Cfg::kTmemCols);
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Host-side dispatch
+// ------------------------------------------------------------------------------------------
+template <int D, bool CAUSAL, int VARIANT>
+cudaError_t launch_cfg(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                       const CUtensorMap& tm_o, const FwdArgs& args, cudaStream_t stream) {
+    using Cfg = FwdCfg<D, CAUSAL, VARIANT>;
+    auto* kernel = fa_fwd_sm100_kernel<Cfg>;
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           Cfg::kSmemAlloc);
+    if (err != cudaSuccess) {
+        return err;
+    }
+    const int rows_per_cta = Cfg::NQ * kBM;
+    const dim3 grid(static_cast<unsigned>((args.seqlen + rows_per_cta - 1) / rows_per_cta),
+                    static_cast<unsigned>(args.num_bh));
+    kernel<<<grid, Cfg::kThreads, Cfg::kSmemAlloc, stream>>>(tm_q, tm_k, tm_v, tm_o, args);
+    return cudaGetLastError();
+}
+
+template <int D, bool CAUSAL>
+cudaError_t launch_variant(int variant, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                           const CUtensorMap& tm_v, const CUtensorMap& tm_o, const FwdArgs& args,
+                           cudaStream_t stream) {
+    switch (variant) {
+        case kVariantBaseline:
+            return launch_cfg<D, CAUSAL, kVariantBaseline>(tm_q, tm_k, tm_v, tm_o, args, stream);
+        case kVariantOpt:
+            return launch_cfg<D, CAUSAL, kVariantOpt>(tm_q, tm_k, tm_v, tm_o, args, stream);
+        case kVariantFp16Acc:
+            return launch_cfg<D, CAUSAL, kVariantFp16Acc>(tm_q, tm_k, tm_v, tm_o, args, stream);
+        default:
+            return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_forward(int head_dim, bool causal, int variant, const CUtensorMap& tm_q,
+                           const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                           const CUtensorMap& tm_o, const FwdArgs& args, cudaStream_t stream) {
+    if (head_dim == 64) {
+        return causal ? launch_variant<64, true>(variant, tm_q, tm_k, tm_v, tm_o, args, stream)
+                      : launch_variant<64, false>(variant, tm_q, tm_k, tm_v, tm_o, args, stream);
+    }
+    if (head_dim == 128) {
+        return causal ? launch_variant<128, true>(variant, tm_q, tm_k, tm_v, tm_o, args, stream)
+                      : launch_variant<128, false>(variant, tm_q, tm_k, tm_v, tm_o, args, stream);
+    }
+    return cudaErrorInvalidValue;
+}
+
+template <int D>
+int smem_for(int variant) {
+    switch (variant) {
+        case kVariantBaseline:
+            return FwdCfg<D, false, kVariantBaseline>::kSmemAlloc;
+        case kVariantOpt:
+            return FwdCfg<D, false, kVariantOpt>::kSmemAlloc;
+        default:
+            return FwdCfg<D, false, kVariantFp16Acc>::kSmemAlloc;
+    }
+}
+
+template <int D>
+int threads_for(int variant) {
+    switch (variant) {
+        case kVariantBaseline:
+            return FwdCfg<D, false, kVariantBaseline>::kThreads;
+        case kVariantOpt:
+            return FwdCfg<D, false, kVariantOpt>::kThreads;
+        default:
+            return FwdCfg<D, false, kVariantFp16Acc>::kThreads;
+    }
+}
+
+int kernel_smem_bytes(int head_dim, bool /*causal*/, int variant) {
+    return head_dim == 64 ? smem_for<64>(variant) : smem_for<128>(variant);
+}
+
+int kernel_threads(int head_dim, bool /*causal*/, int variant) {
+    return head_dim == 64 ? threads_for<64>(variant) : threads_for<128>(variant);
+}
+
+}  // namespace fa_sm100

@@ -1,0 +1,343 @@
+#pragma once
+// Inline-PTX building blocks for sm_100a (B200): mbarriers with bounded waits, TMA tensor
+// loads/stores, tcgen05 MMA with TMEM accumulators, TMEM load/store, and the shared-memory /
+// instruction descriptors those MMAs take.
+//
+// This header replaces the sm_80 helper set of the reference (csrc/common.cuh:57-142:
+// cp.async, ldmatrix, mma.sync, ex2.f16x2). Nothing here is a translation of it: the data
+// movement is TMA + mbarrier, the contraction is tcgen05.mma, and the accumulators live in
+// tensor memory instead of registers.
+//
+// Descriptor bit layouts follow the PTX ISA (tcgen05 "shared memory descriptor" and
+// "instruction descriptor" tables); the canonical 128-byte-swizzle layouts are the ones TMA
+// writes with CU_TENSOR_MAP_SWIZZLE_128B.
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+namespace fa_sm100 {
+
+// ------------------------------------------------------------------------------------------
+// Error codes written to the device status word when a bounded wait gives up.
+// ------------------------------------------------------------------------------------------
+enum : unsigned {
+    kStatusOk = 0,
+    kStatusTimeoutProducer = 1u << 0,  // TMA producer waited too long for a free ring slot
+    kStatusTimeoutMma = 1u << 1,       // MMA issuer waited too long for data / P
+    kStatusTimeoutSoftmax = 1u << 2,   // softmax warps waited too long for S / O
+    kStatusTimeoutEpilogue = 1u << 3,  // epilogue store waited too long for its rows
+    kStatusTimeoutTeardown = 1u << 4,  // teardown waited too long for in-flight async work
+};
+
+// A wait gives up after this many nanoseconds of %globaltimer. Every legitimate wait in the
+// kernel is a few microseconds; one second only trips on a real deadlock.
+constexpr unsigned long long kWaitTimeoutNs = 1000ull * 1000ull * 1000ull;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ------------------------------------------------------------------------------------------
+// mbarrier
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Where a bounded wait reports that it gave up.
+struct WaitCtx {
+    volatile int* cta_abort;           // shared flag: some thread of this CTA gave up
+    unsigned* code_word;               // global sticky error bits (host reads and clears)
+    volatile unsigned* epoch_word;     // global: epoch of the last launch that gave up
+    unsigned epoch;                    // this launch's epoch (never 0)
+};
+
+// Bounded wait for the phase with the given parity. Returns false when the wait ran out of
+// time (after setting `code` in the global status, the CTA abort flag and the launch's abort
+// epoch), or when another thread of this CTA or another CTA of this launch has given up.
+// The result is per thread; callers that go on to warp-collective instructions vote on it.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtx& w,
+                                          unsigned code) {
+    if (mbar_try_wait(bar, parity)) {
+        return true;
+    }
+    const unsigned long long t0 = globaltimer_ns();
+    uint32_t spins = 0;
+    while (true) {
+        if (mbar_try_wait(bar, parity)) {
+            return true;
+        }
+        if (*w.cta_abort != 0) {
+            return false;
+        }
+        if ((++spins & 255u) == 0) {
+            if (*w.epoch_word == w.epoch) {
+                *w.cta_abort = 1;
+                return false;
+            }
+            if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+                atomicOr(w.code_word, code);
+                *w.epoch_word = w.epoch;
+                *w.cta_abort = 1;
+                return false;
+            }
+        }
+    }
+}
+
+// Bounded wait used on the way out after an abort: it ignores the abort flags (the point is to
+// let in-flight asynchronous copies / MMAs land before shared or tensor memory is released)
+// and only gives up on time.
+__device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, const WaitCtx& w,
+                                                unsigned code) {
+    const unsigned long long t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+            atomicOr(w.code_word, code);
+            *w.epoch_word = w.epoch;
+            return false;
+        }
+    }
+    return true;
+}
+
+// ------------------------------------------------------------------------------------------
+// TMA (cp.async.bulk.tensor), 3-D tiled, no multicast.
+// Coordinates are {x = element along the contiguous head dim, y = row, z = head}; x is always
+// a multiple of 64 (128 bytes), so every copy starts on a 16-byte boundary.
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int x, int y,
+                                             int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(src), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_store_commit() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Wait until the bulk stores of this thread have finished READING shared memory.
+__device__ __forceinline__ void tma_store_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// Generic-proxy writes to shared memory become visible to the async proxy (TMA store).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ------------------------------------------------------------------------------------------
+// Tensor memory (TMEM). Addresses: bits 31..16 = lane, bits 15..0 = 32-bit column.
+// A warp may only touch lanes [32 * (warp % 4), 32 * (warp % 4) + 32).
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t smem_dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_dst),
+                 "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns: thread i of the warp gets lane (base + i),
+// register c = column (col + c).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+        "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+        "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+        "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+        "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+// ------------------------------------------------------------------------------------------
+// tcgen05.mma, kind::f16 (fp16 x fp16, fp32 or fp16 accumulate), one CTA.
+// ------------------------------------------------------------------------------------------
+// A and B both from shared memory (descriptors).
+__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                        uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// A from tensor memory (16-bit elements packed two per column, K-major), B from shared memory.
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                        uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// The mbarrier gets one arrival once every tcgen05.mma issued so far by this thread is done.
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+        : "memory");
+}
+
+// ------------------------------------------------------------------------------------------
+// Descriptors
+// ------------------------------------------------------------------------------------------
+// Shared-memory matrix descriptor (64 bit):
+//   [0,14)  start address >> 4        [16,30) leading-dimension byte offset >> 4
+//   [32,46) stride-dimension byte offset >> 4
+//   [46,48) version = 1 (tcgen05)     [49,52) base offset = 0 (atoms are 1024-byte aligned)
+//   [61,64) layout: 2 = 128-byte swizzle
+constexpr uint64_t kDescSwizzle128 = 2;
+
+__host__ __device__ constexpr uint64_t make_smem_desc(uint32_t saddr, uint32_t lbo_bytes,
+                                                      uint32_t sbo_bytes) {
+    return (static_cast<uint64_t>((saddr >> 4) & 0x3FFFu)) |
+           (static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16) |
+           (static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32) | (1ull << 46) |
+           (kDescSwizzle128 << 61);
+}
+
+// Operand stored K-major with 128-byte swizzle: rows of 64 fp16 (128 B), 8-row atoms of
+// 1024 B stacked along M/N. LBO is unused for swizzled K-major layouts (encoded as 16 B);
+// SBO = 1024 B between 8-row groups. Stepping K by 16 elements inside an atom adds 32 B to
+// the start address.
+__host__ __device__ constexpr uint64_t make_desc_kmajor_sw128(uint32_t saddr) {
+    return make_smem_desc(saddr, 16, 1024);
+}
+
+// Operand stored MN-major with 128-byte swizzle (V as the B operand of P.V: N = head dim is
+// contiguous). A row of the smem tile is one key (K index) holding 64 head-dim values;
+// SBO = 1024 B between groups of 8 keys, LBO = byte distance between 64-wide head-dim blocks.
+__host__ __device__ constexpr uint64_t make_desc_mnmajor_sw128(uint32_t saddr,
+                                                               uint32_t mn_block_bytes) {
+    return make_smem_desc(saddr, mn_block_bytes, 1024);
+}
+
+// Instruction descriptor for kind::f16 (32 bit):
+//   [4,6) D format (0 = f16, 1 = f32)   [7,10) A format (0 = f16)   [10,13) B format (0 = f16)
+//   [15] A major (0 = K)   [16] B major (0 = K, 1 = MN)   [17,23) N >> 3   [24,29) M >> 4
+__host__ __device__ constexpr uint32_t make_idesc_f16(int m, int n, bool d_f32, bool b_mn_major) {
+    return (static_cast<uint32_t>(d_f32 ? 1 : 0) << 4) |
+           (static_cast<uint32_t>(b_mn_major ? 1 : 0) << 16) |
+           (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// ------------------------------------------------------------------------------------------
+// Arithmetic helpers
+// ------------------------------------------------------------------------------------------
+// 2^x on the special-function unit (flush-to-zero; 2^-inf = +0).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Two 2^x of packed fp16 values in one instruction.
+__device__ __forceinline__ uint32_t ex2_approx_f16x2(uint32_t x) {
+    uint32_t y;
+    asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float2 unpack_half2(uint32_t r) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&r));
+}
+
+}  // namespace fa_sm100

@@ -1,0 +1,165 @@
+"""Python binding of libfa_b200.so (the C ABI in include/fa_b200.h), via ctypes.
+
+Mirrors the reference's Torch binding ``_C.forward`` (csrc/bindings.cpp:28-73, fa/_C.pyi:4-11):
+same signature, same checks in the same order, same messages, same exception types
+(TORCH_CHECK -> RuntimeError; the kernel's std::invalid_argument -> ValueError). The output is
+allocated with ``torch.empty_like(q)`` and the kernel is enqueued on the current CUDA stream of
+q's device; the call does not synchronise.
+
+There is no fallback: if the shared library is missing or fails to load, importing this module
+raises ImportError.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+from pathlib import Path
+
+import torch
+
+_LIB_NAME = "libfa_b200.so"
+_LIB_PATH = Path(os.environ.get("FA_B200_LIB", Path(__file__).resolve().parent / _LIB_NAME))
+
+FA_OK = 0
+FA_ERR_INVALID_ARGUMENT = 1
+FA_ERR_CUDA = 2
+FA_ERR_DEVICE_TIMEOUT = 3
+
+VARIANTS = {"baseline": 0, "opt": 1, "fp16acc": 2}
+
+
+class FaFwdParams(ctypes.Structure):
+    """ctypes image of ``FaFwdParams`` (include/fa_b200.h)."""
+
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("k", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("o", ctypes.c_void_p),
+        ("batch", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("seqlen", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("softmax_scale", ctypes.c_float),
+        ("causal", ctypes.c_uint8),
+        ("variant", ctypes.c_uint8),
+        ("reserved", ctypes.c_uint8 * 2),
+    ]
+
+
+def _load() -> ctypes.CDLL:
+    if not _LIB_PATH.exists():
+        raise ImportError(
+            f"{_LIB_PATH} not found: build it with "
+            "`python flash-attention-from-scratch_b200/build.py` (nvcc, sm_100a)"
+        )
+    lib = ctypes.CDLL(str(_LIB_PATH))
+    lib.fa_flash_fwd.argtypes = [ctypes.POINTER(FaFwdParams), ctypes.c_void_p]
+    lib.fa_flash_fwd.restype = ctypes.c_int
+    lib.fa_flash_fwd_sharded.argtypes = [
+        ctypes.POINTER(FaFwdParams),
+        ctypes.POINTER(ctypes.c_int32),
+        ctypes.POINTER(ctypes.c_void_p),
+        ctypes.c_int32,
+    ]
+    lib.fa_flash_fwd_sharded.restype = ctypes.c_int
+    lib.fa_last_error.argtypes = []
+    lib.fa_last_error.restype = ctypes.c_char_p
+    lib.fa_device_status.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(ctypes.c_uint32)]
+    lib.fa_device_status.restype = ctypes.c_int
+    lib.fa_kernel_info.argtypes = [
+        ctypes.c_int32,
+        ctypes.c_int32,
+        ctypes.POINTER(ctypes.c_int32),
+        ctypes.POINTER(ctypes.c_int32),
+    ]
+    lib.fa_kernel_info.restype = ctypes.c_int
+    return lib
+
+
+lib = _load()
+
+
+def _raise(rc: int) -> None:
+    msg = lib.fa_last_error().decode()
+    if rc == FA_ERR_INVALID_ARGUMENT:
+        raise ValueError(msg)
+    raise RuntimeError(msg or f"flash_fwd failed with code {rc}")
+
+
+def parse_variant(name: str) -> int:
+    """Reference: parse_variant, csrc/bindings.cpp:15-26."""
+    if name in VARIANTS:
+        return VARIANTS[name]
+    raise RuntimeError(f"variant must be 'opt', 'fp16acc' or 'baseline', got '{name}'")
+
+
+def check_inputs(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
+    """The TORCH_CHECKs of csrc/bindings.cpp:31-40, in the same order and wording."""
+    for t in (q, k, v):
+        if not t.is_cuda:
+            raise RuntimeError("q, k, v must be CUDA tensors")
+        if t.dtype != torch.float16:
+            raise RuntimeError("q, k, v must be float16")
+        if not t.is_contiguous():
+            raise RuntimeError("q, k, v must be contiguous")
+        if t.dim() != 4:
+            raise RuntimeError("q, k, v must have shape [B, H, N, D]")
+    if q.shape != k.shape or q.shape != v.shape:
+        raise RuntimeError("q, k, v must have the same shape")
+    if q.device != k.device or q.device != v.device:
+        raise RuntimeError("q, k, v must be on the same device")
+
+
+def make_params(q, k, v, o, causal: bool, softmax_scale: float, variant: int) -> FaFwdParams:
+    p = FaFwdParams()
+    p.q, p.k, p.v, p.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr()
+    p.batch, p.heads, p.seqlen, p.head_dim = (int(x) for x in q.shape)
+    p.softmax_scale = float(softmax_scale)
+    p.causal = 1 if causal else 0
+    p.variant = variant
+    return p
+
+
+def forward(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    causal: bool = False,
+    softmax_scale: float | None = None,
+    variant: str = "opt",
+) -> torch.Tensor:
+    """O = softmax(Q K^T * scale) V (reference csrc/bindings.cpp:28-64)."""
+    check_inputs(q, k, v)
+    with torch.cuda.device(q.device):
+        o = torch.empty_like(q)
+        head_dim = q.shape[3]
+        scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(head_dim)
+        vid = parse_variant(variant)
+        if q.shape[2] > 0:
+            params = make_params(q, k, v, o, causal, scale, vid)
+            stream = torch.cuda.current_stream(q.device).cuda_stream
+            rc = lib.fa_flash_fwd(ctypes.byref(params), ctypes.c_void_p(stream))
+            if rc != FA_OK:
+                _raise(rc)
+    return o
+
+
+def device_status(device: int, clear: bool = True) -> int:
+    """Sticky watchdog bits of `device` (0 = no kernel gave up a wait). Synchronises."""
+    out = ctypes.c_uint32(0)
+    rc = lib.fa_device_status(int(device), 1 if clear else 0, ctypes.byref(out))
+    if rc != FA_OK:
+        _raise(rc)
+    return int(out.value)
+
+
+def kernel_info(head_dim: int, variant: str = "opt") -> tuple[int, int]:
+    """(shared-memory bytes, threads) per CTA of the kernel for (head_dim, variant)."""
+    smem, thr = ctypes.c_int32(0), ctypes.c_int32(0)
+    rc = lib.fa_kernel_info(int(head_dim), parse_variant(variant), ctypes.byref(smem), ctypes.byref(thr))
+    if rc != FA_OK:
+        _raise(rc)
+    return int(smem.value), int(thr.value)

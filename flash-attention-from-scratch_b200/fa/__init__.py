@@ -1,0 +1,44 @@
+"""FlashAttention-2 forward for NVIDIA B200 (sm_100a), written from scratch.
+
+    import fa
+    o = fa.forward(q, k, v, causal=False)      # q, k, v: [B, H, N, D] fp16 CUDA, D in {64, 128}
+    o = fa.forward(q, k, v, fp16_accum=True)   # P.V accumulated in fp16 per 64 keys
+
+Same public surface as the reference package (fa/__init__.py:14-38): ``forward``,
+``forward_variant`` and ``attention_reference``. The kernel is tcgen05 / TMEM / TMA code for
+sm_100a in libfa_b200.so; there is no CPU or fallback path.
+"""
+
+import torch
+
+from fa import _C
+from fa.reference import attention_reference
+from fa.shard import forward_sharded, plan_shards
+
+
+def forward(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    causal: bool = False,
+    softmax_scale: float | None = None,
+    fp16_accum: bool = False,
+) -> torch.Tensor:
+    """O = softmax(Q K^T * scale) V.
+
+    fp16_accum: accumulate P @ V in fp16 within each 64-key half tile (folded into fp32
+    between them), the reference's "fp16acc" build. On B200 it runs no faster than fp32
+    accumulation; it exists for API and numerical parity.
+    """
+    variant = "fp16acc" if fp16_accum else "opt"
+    return _C.forward(q, k, v, causal, softmax_scale, variant)
+
+
+def forward_variant(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False, variant: str = "opt"
+) -> torch.Tensor:
+    """Run a specific kernel build: 'baseline', 'opt' or 'fp16acc' (benchmarks, tests)."""
+    return _C.forward(q, k, v, causal, None, variant)
+
+
+__all__ = ["forward", "forward_variant", "attention_reference", "forward_sharded", "plan_shards"]

@@ -1,0 +1,94 @@
+/* C ABI of the B200 (sm_100a) FlashAttention-2 forward library, libfa_b200.so.
+ *
+ * Plain C: raw device pointers, sizes and a CUDA stream handle, no PyTorch or C++ types, so a
+ * ctypes / cgo / JNI / N-API binding can call it directly. Every entry point is re-entrant and
+ * thread-safe; the library keeps no per-call state and allocates no device memory per call.
+ *
+ * Reference interfaces each entry point replaces (aligoldenhat/flash-attention-from-scratch):
+ *   FaFwdParams          <- fa::FlashFwdParams          csrc/flash_fwd.h:18-30
+ *   FA_VARIANT_*         <- fa::Variant                 csrc/flash_fwd.h:12-16
+ *   fa_flash_fwd()       <- fa::flash_fwd()             csrc/flash_fwd.h:32-33,
+ *                                                       csrc/kernels/flash_fwd.cu:625-652
+ *   fa_last_error()      <- the what() string of the std::invalid_argument / runtime_error
+ *                           that fa::flash_fwd throws (csrc/kernels/flash_fwd.cu:626-651,
+ *                           csrc/common.cuh:15-26); a C ABI cannot throw.
+ */
+#ifndef FA_B200_H_
+#define FA_B200_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FA_API __attribute__((visibility("default")))
+#else
+#define FA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same layout as cudaStream_t / CUstream; NULL is the legacy default stream. */
+struct CUstream_st;
+typedef struct CUstream_st* fa_stream_t;
+
+/* Return codes. */
+#define FA_OK 0
+#define FA_ERR_INVALID_ARGUMENT 1 /* reference: std::invalid_argument (Python ValueError) */
+#define FA_ERR_CUDA 2             /* reference: std::runtime_error from CUDA_CHECK        */
+#define FA_ERR_DEVICE_TIMEOUT 3   /* a kernel gave up a bounded wait (see fa_device_status) */
+
+/* Kernel builds (reference csrc/flash_fwd.h:12-16). */
+#define FA_VARIANT_BASELINE 0 /* exact running max, fp32 accumulation                      */
+#define FA_VARIANT_OPT 1      /* lazy rescale (threshold 2^8), fp32 accumulation (default)  */
+#define FA_VARIANT_FP16ACC 2  /* P.V accumulated in fp16 per 64 keys, folded into fp32      */
+
+/* Forward parameters (reference fa::FlashFwdParams, csrc/flash_fwd.h:18-30).
+ * q, k, v, o: [batch, heads, seqlen, head_dim] fp16, contiguous, 16-byte aligned, on the
+ * current CUDA device. o is written; the caller owns every buffer. */
+typedef struct FaFwdParams {
+    const void* q;
+    const void* k;
+    const void* v;
+    void* o;
+    int32_t batch;
+    int32_t heads;
+    int32_t seqlen;   /* N, queries == keys */
+    int32_t head_dim; /* 64 or 128 */
+    float softmax_scale;
+    uint8_t causal;
+    uint8_t variant; /* FA_VARIANT_* */
+    uint8_t reserved[2];
+} FaFwdParams;
+
+/* Enqueues O = softmax(Q K^T * scale) V on `stream` (current device). Asynchronous: no host
+ * synchronisation. Validates like the reference (batch, heads, seqlen > 0; head_dim 64/128;
+ * batch*heads <= 65535; 16-byte aligned pointers; known variant) and returns
+ * FA_ERR_INVALID_ARGUMENT with a message in fa_last_error() on failure.
+ * Reference: fa::flash_fwd, csrc/kernels/flash_fwd.cu:625-652. */
+FA_API int fa_flash_fwd(const FaFwdParams* params, fa_stream_t stream);
+
+/* Host-side head-sharding launcher: shard i is enqueued on device devices[i] and stream
+ * streams[i] (each shard a complete [b, h, N, d] problem already resident on that device).
+ * No collective: heads are independent. Returns the first error; later shards are not
+ * launched after an error. Replaces the single-GPU launch loop of bench/benchmark.py:108-120
+ * for multi-GPU runs (the reference has no multi-GPU code). */
+FA_API int fa_flash_fwd_sharded(const FaFwdParams* shards, const int32_t* devices,
+                         const fa_stream_t* streams, int32_t num_shards);
+
+/* Message of the last error on the calling thread ("" if none). */
+FA_API const char* fa_last_error(void);
+
+/* Reads (and if clear != 0, clears) the sticky device watchdog bits of `device`: nonzero
+ * means a kernel gave up a bounded wait instead of hanging, and its output is not valid.
+ * Synchronises the device. Returns FA_OK and writes the bits to *status_out. */
+FA_API int fa_device_status(int32_t device, int32_t clear, uint32_t* status_out);
+
+/* Shared memory bytes and threads per CTA of the kernel used for (head_dim, variant). */
+FA_API int fa_kernel_info(int32_t head_dim, int32_t variant, int32_t* smem_bytes, int32_t* threads);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FA_B200_H_ */

@@ -1,0 +1,55 @@
+"""Shared helpers of the GPU parity tests: error statistics, the tolerances, and a fp32 torch
+reference evaluated head-chunk by head-chunk on the GPU for shapes whose N x N scores do not
+fit at once."""
+
+from __future__ import annotations
+
+import torch
+
+import fa
+
+# BASELINE north_star tolerances against fa/reference.py (fp32 oracle).
+MAX_ABS_FP32 = 2e-3
+MEAN_ABS_FP32 = 2e-4
+MAX_ABS_FP16ACC = 1e-2
+# The reference's own test tolerance (tests/test_flash_fwd.py:12-13).
+REF_ATOL = 1e-2
+REF_RTOL = 1e-2
+
+
+def err_stats(out: torch.Tensor, ref: torch.Tensor) -> tuple[float, float]:
+    diff = (out.float() - ref.float()).abs()
+    return float(diff.max()), float(diff.mean())
+
+
+def fp16_floor(ref: torch.Tensor) -> float:
+    """Max error of the exact result merely rounded to fp16: no fp16 kernel can beat it."""
+    return float((ref.half().float() - ref.float()).abs().max())
+
+
+def check_tolerance(out, ref, variant: str, label: str = "") -> tuple[float, float]:
+    mx, mean = err_stats(out, ref)
+    if variant == "fp16acc":
+        assert mx <= MAX_ABS_FP16ACC, f"{label} fp16acc max-abs {mx:.3e} > {MAX_ABS_FP16ACC}"
+    else:
+        floor = fp16_floor(ref)
+        assert mx <= max(MAX_ABS_FP32, floor), f"{label} max-abs {mx:.3e} > {MAX_ABS_FP32} (fp16 floor {floor:.3e})"
+        assert mean <= MEAN_ABS_FP32, f"{label} mean-abs {mean:.3e} > {MEAN_ABS_FP32}"
+    return mx, mean
+
+
+@torch.no_grad()
+def gpu_reference(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, budget_bytes: int = 4 << 30) -> torch.Tensor:
+    """fa.attention_reference (fp32, tf32 off) over chunks of heads, on q's device."""
+    b, h, n, d = q.shape
+    qf, kf, vf = (t.reshape(b * h, 1, n, d) for t in (q, k, v))
+    out = torch.empty((b * h, 1, n, d), dtype=torch.float32, device=q.device)
+    chunk = max(1, budget_bytes // max(1, 3 * n * n * 4))
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        for i in range(0, b * h, chunk):
+            out[i : i + chunk] = fa.attention_reference(qf[i : i + chunk], kf[i : i + chunk], vf[i : i + chunk], causal)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    return out.reshape(b, h, n, d)

@@ -1,0 +1,103 @@
+"""The C ABI (include/fa_b200.h) without a GPU: the library loads, exports every declared entry
+point, its struct layout matches what a C compiler makes of the header, and argument validation
+mirrors the reference's fa::flash_fwd (csrc/kernels/flash_fwd.cu:625-651) -- all of which runs
+before any CUDA call."""
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from fa import _C
+
+REPO = Path(__file__).resolve().parent.parent
+HEADER = REPO / "include" / "fa_b200.h"
+
+
+def _declared_functions():
+    text = HEADER.read_text()
+    return re.findall(r"FA_API\s+[\w\s\*]+?\b(fa_\w+)\s*\(", text)
+
+
+def test_header_declares_entry_points():
+    names = _declared_functions()
+    assert set(names) >= {"fa_flash_fwd", "fa_flash_fwd_sharded", "fa_last_error", "fa_device_status", "fa_kernel_info"}
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(str(_C._LIB_PATH))
+    for name in _declared_functions():
+        assert hasattr(lib, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_C._LIB_PATH)], capture_output=True, text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    assert set(_declared_functions()) <= exported
+
+
+def test_params_struct_layout_matches_c_header(tmp_path):
+    src = tmp_path / "layout.c"
+    src.write_text(
+        '#include <stdio.h>\n#include <stddef.h>\n#include "fa_b200.h"\n'
+        "int main(void){printf(\"%zu %zu %zu %zu %zu %zu %zu %zu\\n\", sizeof(FaFwdParams),"
+        " offsetof(FaFwdParams,o), offsetof(FaFwdParams,batch), offsetof(FaFwdParams,seqlen),"
+        " offsetof(FaFwdParams,head_dim), offsetof(FaFwdParams,softmax_scale),"
+        " offsetof(FaFwdParams,causal), offsetof(FaFwdParams,variant)); return 0;}\n"
+    )
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c99", "-I", str(REPO / "include"), "-o", str(exe), str(src)], check=True)
+    got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    P = _C.FaFwdParams
+    want = [ctypes.sizeof(P), P.o.offset, P.batch.offset, P.seqlen.offset, P.head_dim.offset,
+            P.softmax_scale.offset, P.causal.offset, P.variant.offset]
+    assert got == want
+
+
+def _params(**kw):
+    p = _C.FaFwdParams()
+    p.q, p.k, p.v, p.o = 0x10000, 0x20000, 0x30000, 0x40000  # never dereferenced: validation fails first
+    p.batch, p.heads, p.seqlen, p.head_dim = 1, 1, 64, 64
+    p.softmax_scale, p.causal, p.variant = 0.125, 0, 1
+    for k, v in kw.items():
+        setattr(p, k, v)
+    return p
+
+
+@pytest.mark.parametrize(
+    "kw, msg",
+    [
+        (dict(head_dim=32), "head_dim must be 64 or 128, got 32"),
+        (dict(seqlen=0), "must be positive"),
+        (dict(batch=0), "must be positive"),
+        (dict(batch=300, heads=300), "65535"),
+        (dict(q=0x10002), "16-byte aligned"),
+        (dict(variant=7), "unknown variant"),
+    ],
+)
+def test_validation_rejects(kw, msg):
+    rc = _C.lib.fa_flash_fwd(ctypes.byref(_params(**kw)), None)
+    assert rc == _C.FA_ERR_INVALID_ARGUMENT
+    assert msg in _C.lib.fa_last_error().decode()
+
+
+def test_validation_maps_to_value_error():
+    with pytest.raises(ValueError, match="head_dim"):
+        _C._raise(_C.lib.fa_flash_fwd(ctypes.byref(_params(head_dim=96)), None))
+
+
+def test_sharded_rejects_bad_list():
+    rc = _C.lib.fa_flash_fwd_sharded(None, None, None, 3)
+    assert rc == _C.FA_ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("variant", ["baseline", "opt", "fp16acc"])
+def test_kernel_info(d, variant):
+    smem, threads = _C.kernel_info(d, variant)
+    assert 114 * 1024 < smem <= 227 * 1024  # one CTA per SM, within the opt-in limit
+    assert threads in (192, 320)
+
+
+def test_parse_variant_message():
+    with pytest.raises(RuntimeError, match="variant must be 'opt', 'fp16acc' or 'baseline', got 'x'"):
+        _C.parse_variant("x")

@@ -1,0 +1,61 @@
+"""Building-block probe of the sm_100a data path (libfa_selftest.so): TMA 3-D loads into
+128-byte-swizzled smem, K-major / MN-major UMMA descriptors, tcgen05.mma SS and TS, the fp16
+accumulator cell layout in TMEM, tcgen05.ld/st and the swizzled TMA store. Small-integer inputs
+make every expected value exact, so the comparisons are exact (as in the reference's
+tests/cpp/test_ptx.cu exact-equality layout tests)."""
+
+import ctypes
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+LIB = Path(__file__).resolve().parent.parent / "flash-attention-from-scratch_b200" / "fa" / "libfa_selftest.so"
+
+
+def _lib():
+    lib = ctypes.CDLL(str(LIB))
+    lib.fa_selftest_umma.argtypes = [ctypes.c_void_p] * 9 + [ctypes.c_int]
+    lib.fa_selftest_umma.restype = ctypes.c_int
+    lib.fa_selftest_error.restype = ctypes.c_char_p
+    return lib
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_umma_probe_exact(d):
+    g = torch.Generator().manual_seed(100 + d)
+    q = torch.randint(-2, 3, (128, d), generator=g).half()
+    k = torch.randint(-2, 3, (128, d), generator=g).half()
+    v = torch.randint(-2, 3, (128, d), generator=g).half()
+    p = (torch.randint(0, 3, (128, 128), generator=g).float() * 0.5).half()
+    dev = torch.device("cuda:0")
+    qd, kd, vd, pd = (t.to(dev).contiguous() for t in (q, k, v, p))
+    s_out = torch.full((128, 128), float("nan"), device=dev)
+    o_out = torch.full((128, d), float("nan"), device=dev)
+    o16 = torch.zeros((128, d), dtype=torch.int32, device=dev)
+    o_half = torch.zeros((128, d), dtype=torch.float16, device=dev)
+    flags = torch.zeros(2, dtype=torch.int32, device=dev)
+    lib = _lib()
+    rc = lib.fa_selftest_umma(
+        qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), pd.data_ptr(), s_out.data_ptr(), o_out.data_ptr(),
+        o16.data_ptr(), o_half.data_ptr(), flags.data_ptr(), d,
+    )
+    assert rc == 0, lib.fa_selftest_error().decode()
+    assert flags.tolist() == [1, 1]
+    s_ref = q.float() @ k.float().T
+    o_ref = p.float() @ v.float()
+    s_got = s_out.cpu()
+    o_got = o_out.cpu()
+    # Diagnose before asserting: which operand layout is off.
+    assert torch.equal(s_got, s_ref), f"S = Q K^T mismatch: max err {(s_got - s_ref).abs().max()}"
+    assert torch.equal(o_got, o_ref), f"O = P V (fp32 acc) mismatch: max err {(o_got - o_ref).abs().max()}"
+    cells = o16.cpu().numpy().view(np.uint32)
+    lo = (cells & 0xFFFF).astype(np.uint16).view(np.float16).astype(np.float32)
+    hi = (cells >> 16).astype(np.uint16).view(np.float16).astype(np.float32)
+    lo_ok = np.array_equal(lo, o_ref.numpy())
+    hi_ok = np.array_equal(hi, o_ref.numpy())
+    assert lo_ok, f"fp16 accumulator not in the low half of each TMEM cell (high half matches: {hi_ok})"
+    assert torch.equal(o_half.cpu().float(), o_ref), "TMA store of the swizzled fp16 tile mismatch"
