@@ -11,27 +11,26 @@
 // "fp16acc") is the reference's, the machine mapping is new:
 //
 // CTA = one (b,h) head x NQ consecutive 128-row query tiles (NQ = 2, or 1 for fp16acc).
-// Warp roles (warp-specialised, one CTA per SM):
-//   warps 0 .. 4*NQ-1   softmax warpgroup t = warp/4 owns query tile t; thread i of the
-//                       warpgroup owns TMEM lane i = query row i of the tile. Row max and
-//                       row sum need no shuffles. It also rescales O in TMEM when its running
-//                       max moves, and runs the epilogue of its tile.
-//   warp 4*NQ           TMA producer: Q tiles once, then K_0, V_0, K_1, V_1, ... through a
-//                       STAGES-deep ring of 128 x D tiles in 128-byte-swizzled shared memory.
-//   warp 4*NQ+1         MMA issuer (one thread): S_t = Q_t K_j^T (SS MMA, M=128 N=128) into
-//                       TMEM; O_t += P_t V_j (TS MMA: P from TMEM, V from smem, N = D).
+// Warp roles (warp-specialised, one CTA per SM, whole warpgroups):
+//   warpgroup t < NQ    softmax for query tile t; thread i of the warpgroup owns TMEM lane i
+//                       = query row i of the tile, so row max and row sum need no shuffles.
+//                       It also rescales O in TMEM when its running max moves, and runs the
+//                       epilogue of its tile.
+//   warpgroup NQ        warp 0: TMA producer (Q tiles once, then K_0, V_0, K_1, V_1, ...
+//                       through a STAGES-deep ring of 128 x D tiles, 128-byte swizzle);
+//                       warp 1: MMA issuer (one thread) and TMEM allocation; warps 2-3 idle.
+//   With NQ = 2 the softmax warpgroups raise their register limit (setmaxnreg) with the
+//   registers the producer/MMA warpgroup gives up.
 //
 // Tensor memory (512 columns x 128 lanes, fp32 cells):
-//   S_t  columns [128 t, 128 t + 128)        scores of tile t, fp32
-//   P_t  columns [128 t, 128 t + 64)         probabilities, fp16 packed 2 per column,
-//                                            written over S_t once S_t has been read
-//   O_t  columns [128 NQ + D t, ... + D)     fp32 output accumulator of tile t
-//   T_h  columns [128 NQ + D NQ + D h, ...)  fp16acc only: fp16 partial of P.V over keys
-//                                            [64 h, 64 h + 64) of the current K/V tile
-//
-// The MMA issuer orders, per key tile j:  PV_0(j), S_0(j+1), PV_1(j), S_1(j+1). S_t(j+1) is
-// issued after PV_t(j), which reads P_t(j) from the same columns (tcgen05.mma operations of
-// one thread execute in issue order).
+//   S_t  columns [128 t, 128 t + 128)   scores of tile t, fp32
+//   O_t  columns [128 NQ + D t, +D)     fp32 output accumulator of tile t
+//   P_t  (d = 128) columns [128 t, +64) over S_t once S_t has been read: S_t(j+1) is issued
+//        after PV_t(j), and tcgen05.mma operations of one thread execute in issue order;
+//        (d = 64) its own columns [128 NQ + D NQ + 64 t, +64), so that S_t(j+1) can run while
+//        the softmax of tile j is still computing P_t(j).
+//   T_h  (fp16acc) columns [128 NQ + D NQ + D h, +D): fp16 partial of P.V over keys
+//        [64 h, 64 h + 64) of the current K/V tile.
 
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -41,6 +40,21 @@
 
 #include "fa_internal.h"
 #include "sm100_ptx.cuh"
+
+// Software-exp2 share (how many of every 8 column pairs of a 128-key tile take exp2_poly2
+// instead of ex2.approx); compile-time tuning knobs.
+#ifndef FA_EMU_PER8_D128
+#define FA_EMU_PER8_D128 2
+#endif
+#ifndef FA_EMU_PER8_D64
+#define FA_EMU_PER8_D64 3
+#endif
+// Register split between the softmax warpgroups and the producer/MMA warpgroup (NQ = 2):
+// 0 keeps every warp at the launch allocation (168); otherwise softmax warps go to this many
+// and the other warpgroup gives up the difference.
+#ifndef FA_REGS_SOFTMAX
+#define FA_REGS_SOFTMAX 0
+#endif
 
 namespace fa_sm100 {
 
@@ -61,6 +75,8 @@ struct FwdCfg {
     // tile max exceeds it by more than 2^8. Threshold 0 = exact running max.
     static constexpr float kRescaleThreshold = (VARIANT_ == kVariantOpt) ? 8.0f : 0.0f;
     static constexpr int NQ = ACC16 ? 1 : 2;
+    static constexpr bool SEP_P = !ACC16 && D == 64;
+    static constexpr int kEmuPer8 = ACC16 ? 0 : (D == 128 ? FA_EMU_PER8_D128 : FA_EMU_PER8_D64);
     static constexpr int kTileBytes = kBM * D * 2;  // one Q, K, V or O tile (BM == BN)
     static constexpr int kBoxes = D / 64;           // TMA boxes per tile
     static constexpr int STAGES = (D == 128) ? 4 : 8;
@@ -72,15 +88,25 @@ struct FwdCfg {
     // Tensor memory columns.
     static constexpr int kTmemS = 0;
     static constexpr int kTmemO = NQ * kBN;
-    static constexpr int kTmemT = kTmemO + NQ * D;
-    static constexpr int kTmemUsed = kTmemT + (ACC16 ? 2 * D : 0);
+    static constexpr int kTmemExtra = kTmemO + NQ * D;  // P_t (SEP_P) or T_h (ACC16)
+    static constexpr int kTmemUsed = kTmemExtra + (ACC16 ? 2 * D : (SEP_P ? NQ * 64 : 0));
     static constexpr int kTmemCols = 512;
     static_assert(kTmemUsed <= kTmemCols, "tensor memory budget");
-    // Warps.
+    // Warps: NQ softmax warpgroups + one producer/MMA warpgroup.
     static constexpr int kSoftmaxWarps = 4 * NQ;
     static constexpr int kProducerWarp = kSoftmaxWarps;
     static constexpr int kMmaWarp = kSoftmaxWarps + 1;
-    static constexpr int kThreads = 32 * (kSoftmaxWarps + 2);
+    static constexpr int kThreads = 32 * (kSoftmaxWarps + 4);
+    // Register split (NQ = 2, 384 threads launched at 168 each): softmax warpgroups to
+    // kRegsSoftmax, the producer/MMA warpgroup to what is left (multiple of 8).
+    static constexpr int kRegsLaunch = 168;
+    static constexpr int kRegsSoftmax = FA_REGS_SOFTMAX;
+    static constexpr int kRegsOther =
+        kRegsSoftmax == 0 ? kRegsLaunch : ((kThreads * kRegsLaunch - 256 * kRegsSoftmax) / 128) / 8 * 8;
+    static_assert(kRegsSoftmax == 0 || NQ != 2 ||
+                      (256 * kRegsSoftmax + 128 * kRegsOther <= kThreads * kRegsLaunch &&
+                       kRegsOther >= 24 && kRegsSoftmax % 8 == 0 && kRegsSoftmax <= 256),
+                  "register split exceeds the launch allocation");
     static_assert(D == 64 || D == 128, "head dim");
     static_assert(kSmemAlloc <= 227 * 1024, "shared memory budget");
     static_assert(kSmemAlloc > 114 * 1024, "one CTA per SM (it owns all 512 TMEM columns)");
@@ -91,6 +117,7 @@ struct SharedBarriers {
     uint64_t kv_full[8];
     uint64_t kv_empty[8];
     uint64_t s_full[2];
+    uint64_t s_free[2];
     uint64_t p_full[2];
     uint64_t o_done[2];
     uint64_t epi[2];
@@ -146,6 +173,32 @@ __device__ __forceinline__ void issue_pv_mma_f16(uint32_t tmem_t, uint32_t tmem_
     }
 }
 
+// Row max (or min, for a negative scale) of 128 scores: eight independent three-input chains.
+template <bool MAX>
+__device__ __forceinline__ float row_extreme(const uint32_t (&sr)[kBN]) {
+    float m[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        m[i] = u2f(sr[i]);
+    }
+    // Columns 8 .. 119 two groups of 8 at a time, then 120 .. 127.
+    static_assert(kBN == 128, "the reduction below is written for 128 columns");
+#pragma unroll
+    for (int c = 8; c + 16 <= kBN; c += 16) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            m[i] = MAX ? fmax3(m[i], u2f(sr[c + i]), u2f(sr[c + 8 + i]))
+                       : fmin3(m[i], u2f(sr[c + i]), u2f(sr[c + 8 + i]));
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        m[i] = MAX ? fmaxf(m[i], u2f(sr[kBN - 8 + i])) : fminf(m[i], u2f(sr[kBN - 8 + i]));
+    }
+    return MAX ? fmax3(fmax3(m[0], m[1], m[2]), fmax3(m[3], m[4], m[5]), fmaxf(m[6], m[7]))
+               : fmin3(fmin3(m[0], m[1], m[2]), fmin3(m[3], m[4], m[5]), fminf(m[6], m[7]));
+}
+
 template <class Cfg>
 __global__ void __launch_bounds__(Cfg::kThreads, 1)
     fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -188,6 +241,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         for (int t = 0; t < NQ; ++t) {
             mbar_init(smem_u32(&sb.q_full[t]), 1);
             mbar_init(smem_u32(&sb.s_full[t]), 1);
+            mbar_init(smem_u32(&sb.s_free[t]), 128);
             mbar_init(smem_u32(&sb.p_full[t]), 128);
             mbar_init(smem_u32(&sb.o_done[t]), 1);
             mbar_init(smem_u32(&sb.epi[t]), 128);
@@ -214,6 +268,14 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = sb.tmem_base;
 
+    if constexpr (NQ == 2 && Cfg::kRegsSoftmax != 0) {
+        if (warp < Cfg::kSoftmaxWarps) {
+            asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(Cfg::kRegsSoftmax));
+        } else {
+            asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Cfg::kRegsOther));
+        }
+    }
+
     if (warp < Cfg::kSoftmaxWarps) {
         // ================================ softmax warpgroups ================================
         const int t = warp / 4;
@@ -223,8 +285,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         const uint32_t lane_off = static_cast<uint32_t>((warp % 4) * 32) << 16;
         const uint32_t t_s = tmem + lane_off + Cfg::kTmemS + t * kBN;
         const uint32_t t_o = tmem + lane_off + Cfg::kTmemO + t * D;
-        const uint32_t t_t = tmem + lane_off + Cfg::kTmemT;
+        const uint32_t t_p = Cfg::SEP_P ? (tmem + lane_off + Cfg::kTmemExtra + t * 64) : t_s;
+        const uint32_t t_t = tmem + lane_off + Cfg::kTmemExtra;
         const uint32_t bar_s = smem_u32(&sb.s_full[t]);
+        const uint32_t bar_sf = smem_u32(&sb.s_free[t]);
         const uint32_t bar_p = smem_u32(&sb.p_full[t]);
         const uint32_t bar_o = smem_u32(&sb.o_done[t]);
         const float scale_log2 = args.scale_log2;
@@ -248,6 +312,11 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 tmem_ld32(t_s + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
             }
             tmem_wait_ld();
+            if constexpr (Cfg::SEP_P) {
+                // S_t is in registers: the MMA warp may overwrite it with S_t(j+1).
+                tc_fence_before();
+                mbar_arrive(bar_sf);
+            }
 
             const int kbase = j * kBN;
             // Only the last tile can hold keys >= N, and for causal rows only the last tile
@@ -256,49 +325,17 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             float tile_max;
             float mul;
             if (masked) {
-                // Diagonal / ragged tile: scale first, then mask, so masked scores are -inf
-                // whatever the sign of the scale.
+                // Scale first, then mask, so masked scores are -inf whatever the scale's sign.
                 const int cmax = lim - kbase;
-                float mx[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    mx[i] = -INFINITY;
-                }
 #pragma unroll
                 for (int c = 0; c < kBN; ++c) {
-                    const float x = (c > cmax) ? -INFINITY : u2f(sr[c]) * scale_log2;
-                    sr[c] = f2u(x);
-                    mx[c % 8] = fmaxf(mx[c % 8], x);
+                    sr[c] = f2u((c > cmax) ? -INFINITY : u2f(sr[c]) * scale_log2);
                 }
-                tile_max = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+                tile_max = row_extreme<true>(sr);
                 mul = 1.0f;
             } else {
-                float mx[8];
-                if (scale_log2 >= 0.0f) {
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        mx[i] = u2f(sr[i]);
-                    }
-#pragma unroll
-                    for (int c = 8; c < kBN; ++c) {
-                        mx[c % 8] = fmaxf(mx[c % 8], u2f(sr[c]));
-                    }
-                    tile_max = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                     fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        mx[i] = u2f(sr[i]);
-                    }
-#pragma unroll
-                    for (int c = 8; c < kBN; ++c) {
-                        mx[c % 8] = fminf(mx[c % 8], u2f(sr[c]));
-                    }
-                    tile_max = fminf(fminf(fminf(mx[0], mx[1]), fminf(mx[2], mx[3])),
-                                     fminf(fminf(mx[4], mx[5]), fminf(mx[6], mx[7])));
-                }
-                tile_max *= scale_log2;
+                tile_max = (scale_log2 >= 0.0f ? row_extreme<true>(sr) : row_extreme<false>(sr)) *
+                           scale_log2;
                 mul = scale_log2;
             }
 
@@ -308,50 +345,66 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             const bool grew = (new_max != row_max);
             const float alpha = grew ? ex2_approx(row_max - max_used) : 1.0f;  // 0 on tile 0
             row_max = new_max;
-            const float neg_max = -max_used;
 
-            // Probabilities, packed fp16 pairs, into the S columns (P_t).
-            float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            // P_t(j-1) (d = 64: in its own columns) must have been consumed before P_t(j) is
+            // written; O must hold P.V up to tile j-1 before it is rescaled.
+            const bool need_rescale = (!Cfg::ACC16) && j > 0 && (__any_sync(0xffffffffu, grew) != 0);
+            if ((Cfg::SEP_P && j > 0) || need_rescale) {
+                ok = __all_sync(0xffffffffu,
+                                mbar_wait(bar_o, (j - 1) & 1, wctx, kStatusTimeoutSoftmax));
+                if (!ok) {
+                    break;
+                }
+                tc_fence_after();
+            }
+
+            // Probabilities, packed fp16 pairs, into P_t.
+            const float2 mul2 = make_float2(mul, mul);
+            const float2 neg2 = make_float2(-max_used, -max_used);
+            float2 sum2[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                sum2[i] = make_float2(0.0f, 0.0f);
+            }
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
                 uint32_t pk[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                     const int c = half * 64 + 2 * i;
-                    const float x0 = fmaf(u2f(sr[c]), mul, neg_max);
-                    const float x1 = fmaf(u2f(sr[c + 1]), mul, neg_max);
+                    const float2 x2 = __ffma2_rn(make_float2(u2f(sr[c]), u2f(sr[c + 1])), mul2, neg2);
                     uint32_t h;
                     if constexpr (Cfg::EXP16) {
-                        h = ex2_approx_f16x2(pack_half2(x0, x1));
+                        h = ex2_approx_f16x2(pack_half2(x2.x, x2.y));
+                    } else if ((i % 8) < Cfg::kEmuPer8) {
+                        const float2 e = exp2_poly2(x2);
+                        h = pack_half2(e.x, e.y);
                     } else {
-                        h = pack_half2(ex2_approx(x0), ex2_approx(x1));
+                        h = pack_half2(ex2_approx(x2.x), ex2_approx(x2.y));
                     }
-                    const float2 pf = unpack_half2(h);
-                    part[i % 4] += pf.x + pf.y;
+                    sum2[i % 4] = __fadd2_rn(sum2[i % 4], unpack_half2(h));
                     pk[i] = h;
                 }
-                tmem_st32(t_s + half * 32, pk);
+                tmem_st32(t_p + half * 32, pk);
             }
-            row_sum = row_sum * alpha + ((part[0] + part[1]) + (part[2] + part[3]));
+            const float2 s01 = __fadd2_rn(sum2[0], sum2[1]);
+            const float2 s23 = __fadd2_rn(sum2[2], sum2[3]);
+            const float2 s4 = __fadd2_rn(s01, s23);
+            row_sum = fmaf(row_sum, alpha, s4.x + s4.y);
 
             if constexpr (!Cfg::ACC16) {
-                // Rescale O when some row of this warp moved its max (rare with the lazy rule).
-                // O holds P.V up to tile j-1: wait for that MMA first.
-                if (j > 0 && __any_sync(0xffffffffu, grew)) {
-                    ok = __all_sync(0xffffffffu,
-                                    mbar_wait(bar_o, (j - 1) & 1, wctx, kStatusTimeoutSoftmax));
-                    if (!ok) {
-                        break;
-                    }
-                    tc_fence_after();
+                if (need_rescale) {
+                    const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll
                     for (int c = 0; c < D / 32; ++c) {
                         uint32_t o[32];
                         tmem_ld32(t_o + c * 32, o);
                         tmem_wait_ld();
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) {
-                            o[e] = f2u(u2f(o[e]) * alpha);
+                        for (int e = 0; e < 32; e += 2) {
+                            const float2 v = __fmul2_rn(make_float2(u2f(o[e]), u2f(o[e + 1])), a2);
+                            o[e] = f2u(v.x);
+                            o[e + 1] = f2u(v.y);
                         }
                         tmem_st32(t_o + c * 32, o);
                     }
@@ -502,7 +555,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             }
         }
         __syncwarp();
-    } else {
+    } else if (warp == Cfg::kMmaWarp) {
         // ================================== MMA issuer ====================================
         if (lane == 0) {
             bool ok = true;
@@ -534,49 +587,73 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             for (int j = 0; ok && j < n_max; ++j) {
                 const int v_slot = ring++;
                 const int vs = v_slot % STAGES;
-                ok = mbar_wait(smem_u32(&sb.kv_full[vs]), (v_slot / STAGES) & 1, wctx,
-                               kStatusTimeoutMma);
-                if (!ok) {
-                    break;
-                }
-                tc_fence_after();
                 const bool has_next = (j + 1 < n_max);
                 const int k_slot = has_next ? ring++ : 0;
                 const int ks = k_slot % STAGES;
                 bool k_ready = false;
+                bool v_ready = false;
 #pragma unroll
                 for (int t = 0; t < NQ; ++t) {
                     if (!ok || j >= n_kv[t]) {
                         continue;
                     }
-                    ok = mbar_wait(smem_u32(&sb.p_full[t]), j & 1, wctx, kStatusTimeoutMma);
-                    if (!ok) {
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t tmem_p = tmem + Cfg::kTmemS + t * kBN;
-                    const uint32_t v_addr = kv_addr0 + vs * Cfg::kTileBytes;
-                    if constexpr (Cfg::ACC16) {
-                        issue_pv_mma_f16<Cfg>(tmem + Cfg::kTmemT, tmem_p, v_addr);
-                    } else {
-                        issue_pv_mma_f32<Cfg>(tmem + Cfg::kTmemO + t * Cfg::D, tmem_p, v_addr,
-                                              j == 0);
-                    }
-                    umma_commit(smem_u32(&sb.o_done[t]));
-                    if (j + 1 < n_kv[t]) {
-                        if (!k_ready) {
-                            ok = mbar_wait(smem_u32(&sb.kv_full[ks]), (k_slot / STAGES) & 1, wctx,
-                                           kStatusTimeoutMma);
+                    const bool next_s = (j + 1 < n_kv[t]);
+                    const uint32_t s_addr = tmem + Cfg::kTmemS + t * kBN;
+                    if constexpr (Cfg::SEP_P) {
+                        // S_t(j+1) as soon as the softmax has S_t(j) in registers.
+                        if (next_s) {
+                            ok = mbar_wait(smem_u32(&sb.s_free[t]), j & 1, wctx, kStatusTimeoutMma);
+                            if (ok && !k_ready) {
+                                ok = mbar_wait(smem_u32(&sb.kv_full[ks]), (k_slot / STAGES) & 1,
+                                               wctx, kStatusTimeoutMma);
+                                k_ready = true;
+                            }
                             if (!ok) {
                                 break;
                             }
                             tc_fence_after();
-                            k_ready = true;
+                            issue_s_mma<Cfg>(s_addr, q_addr0 + t * Cfg::kTileBytes,
+                                             kv_addr0 + ks * Cfg::kTileBytes);
+                            umma_commit(smem_u32(&sb.s_full[t]));
                         }
-                        issue_s_mma<Cfg>(tmem + Cfg::kTmemS + t * kBN,
-                                         q_addr0 + t * Cfg::kTileBytes,
-                                         kv_addr0 + ks * Cfg::kTileBytes);
-                        umma_commit(smem_u32(&sb.s_full[t]));
+                    }
+                    ok = mbar_wait(smem_u32(&sb.p_full[t]), j & 1, wctx, kStatusTimeoutMma);
+                    if (ok && !v_ready) {
+                        ok = mbar_wait(smem_u32(&sb.kv_full[vs]), (v_slot / STAGES) & 1, wctx,
+                                       kStatusTimeoutMma);
+                        v_ready = true;
+                    }
+                    if (!ok) {
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t v_addr = kv_addr0 + vs * Cfg::kTileBytes;
+                    if constexpr (Cfg::ACC16) {
+                        issue_pv_mma_f16<Cfg>(tmem + Cfg::kTmemExtra, s_addr, v_addr);
+                    } else if constexpr (Cfg::SEP_P) {
+                        issue_pv_mma_f32<Cfg>(tmem + Cfg::kTmemO + t * Cfg::D,
+                                              tmem + Cfg::kTmemExtra + t * 64, v_addr, j == 0);
+                    } else {
+                        issue_pv_mma_f32<Cfg>(tmem + Cfg::kTmemO + t * Cfg::D, s_addr, v_addr,
+                                              j == 0);
+                    }
+                    umma_commit(smem_u32(&sb.o_done[t]));
+                    if constexpr (!Cfg::SEP_P) {
+                        // S_t(j+1) reuses the columns P_t(j) was read from by the MMAs above.
+                        if (next_s) {
+                            if (!k_ready) {
+                                ok = mbar_wait(smem_u32(&sb.kv_full[ks]), (k_slot / STAGES) & 1,
+                                               wctx, kStatusTimeoutMma);
+                                if (!ok) {
+                                    break;
+                                }
+                                tc_fence_after();
+                                k_ready = true;
+                            }
+                            issue_s_mma<Cfg>(s_addr, q_addr0 + t * Cfg::kTileBytes,
+                                             kv_addr0 + ks * Cfg::kTileBytes);
+                            umma_commit(smem_u32(&sb.s_full[t]));
+                        }
                     }
                 }
                 if (!ok) {

@@ -53,7 +53,6 @@ __global__ void __launch_bounds__(128, 1)
     const uint32_t sk = base + kTile;
     const uint32_t sv = base + 2 * kTile;
     const int warp = threadIdx.x / 32;
-    const int lane = threadIdx.x % 32;
     const int row = threadIdx.x;
     const WaitCtx w{&sh.abort, &g_probe_status.code, &g_probe_status.epoch_aborted, 1u};
 
@@ -177,6 +176,19 @@ __global__ void __launch_bounds__(128, 1)
     }
 }
 
+// Software exp2 (exp2_poly2, two lanes at a time) and the SFU ex2.approx on the same inputs.
+__global__ void exp2_probe_kernel(const float* __restrict__ x, float* __restrict__ poly,
+                                  float* __restrict__ sfu, int n) {
+    const int i = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
+    if (i + 1 < n) {
+        const float2 e = exp2_poly2(make_float2(x[i], x[i + 1]));
+        poly[i] = e.x;
+        poly[i + 1] = e.y;
+        sfu[i] = ex2_approx(x[i]);
+        sfu[i + 1] = ex2_approx(x[i + 1]);
+    }
+}
+
 thread_local std::string g_err;
 
 }  // namespace
@@ -225,6 +237,27 @@ __attribute__((visibility("default"))) int fa_selftest_umma(const void* q, const
     if (err == cudaSuccess) {
         err = cudaGetLastError();
     }
+    if (err == cudaSuccess) {
+        err = cudaDeviceSynchronize();
+    }
+    if (err != cudaSuccess) {
+        g_err = std::string("CUDA error: ") + cudaGetErrorString(err);
+        return 3;
+    }
+    return 0;
+}
+
+// Evaluates the kernel's two exp2 implementations on n (even) device floats. Synchronises.
+__attribute__((visibility("default"))) int fa_selftest_exp2(const float* x, float* poly, float* sfu,
+                                                            int n) {
+    using namespace fa_sm100;
+    if (n <= 0 || (n & 1) != 0) {
+        g_err = "n must be positive and even";
+        return 1;
+    }
+    const int pairs = n / 2;
+    exp2_probe_kernel<<<(pairs + 255) / 256, 256>>>(x, poly, sfu, n);
+    cudaError_t err = cudaGetLastError();
     if (err == cudaSuccess) {
         err = cudaDeviceSynchronize();
     }

@@ -99,10 +99,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const W
         if (mbar_try_wait(bar, parity)) {
             return true;
         }
-        if (*w.cta_abort != 0) {
-            return false;
-        }
-        if ((++spins & 255u) == 0) {
+        // The abort flags and the clock are checked every 32 polls only: a polling warp shares
+        // its SM sub-partition's issue slots with the warps doing the work.
+        if ((++spins & 31u) == 0) {
+            if (*w.cta_abort != 0) {
+                return false;
+            }
             if (*w.epoch_word == w.epoch) {
                 *w.cta_abort = 1;
                 return false;
@@ -322,6 +324,44 @@ __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// 2^x on the FMA pipe for two values (a software alternative to the special-function unit,
+// whose 16 results / clock / SM equal the tensor cores' rate on a 128 x 128 x 128 tile).
+// 2^x = 2^j * 2^f with j = round(x) taken from the low mantissa bits of x + 1.5 * 2^23 and
+// f = x - j in [-1/2, 1/2]; 2^f by a degree-4 polynomial fitted for minimax relative error
+// with Lawson's algorithm (csrc/fit_exp2_poly.py: max relative error 2.9e-6 in float32, far
+// below the 4.9e-4 of the fp16 rounding that follows); 2^j is added into the exponent field.
+// Inputs below -126 are clamped (their 2^x rounds to 0 in fp16 anyway); -inf gives 2^-126.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+    constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+    x.x = fmaxf(x.x, -126.0f);
+    x.y = fmaxf(x.y, -126.0f);
+    const float2 t = __fadd2_rn(x, make_float2(kRound, kRound));
+    const float2 r = __fadd2_rn(t, make_float2(-kRound, -kRound));
+    const float2 f = __ffma2_rn(r, make_float2(-1.0f, -1.0f), x);
+    float2 p = __ffma2_rn(make_float2(0.009582852944731712f, 0.009582852944731712f), f,
+                          make_float2(0.055906426161527634f, 0.055906426161527634f));
+    p = __ffma2_rn(p, f, make_float2(0.24024099111557007f, 0.24024099111557007f));
+    p = __ffma2_rn(p, f, make_float2(0.6931241750717163f, 0.6931241750717163f));
+    p = __ffma2_rn(p, f, make_float2(1.0f, 1.0f));
+    // t's bits are 0x4B400000 + j; shifted left by 23 only j survives (mod 2^9), which adds j to
+    // the exponent of p in [2^-1/2, 2^1/2].
+    return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                       __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+
+// Row-max helper: three-input max.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+    float d;
+    asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
 }
 
 // Two 2^x of packed fp16 values in one instruction.

@@ -59,3 +59,31 @@ def test_umma_probe_exact(d):
     hi_ok = np.array_equal(hi, o_ref.numpy())
     assert lo_ok, f"fp16 accumulator not in the low half of each TMEM cell (high half matches: {hi_ok})"
     assert torch.equal(o_half.cpu().float(), o_ref), "TMA store of the swizzled fp16 tile mismatch"
+
+
+def test_exp2_implementations_error_bounds():
+    """The kernel's software 2^x (exp2_poly2, degree-4 minimax polynomial) and the SFU
+    ex2.approx, against exp2 in double, over the range the softmax uses ([-126, 8] plus the
+    masked -inf). Bound for the polynomial: 2.9e-6 fitted + float32 rounding; both far below the
+    fp16 rounding (4.9e-4) applied to P afterwards."""
+    lib = ctypes.CDLL(str(LIB))
+    lib.fa_selftest_exp2.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int]
+    lib.fa_selftest_error.restype = ctypes.c_char_p
+    x = torch.cat([torch.linspace(-126.0, 8.0, 1 << 20), torch.tensor([0.0, 1.0, -1.0, 8.0, -0.5, 0.5, float("-inf"), -200.0])])
+    x = x[: (x.numel() // 2) * 2].float()
+    xd = x.cuda()
+    poly = torch.empty_like(xd)
+    sfu = torch.empty_like(xd)
+    assert lib.fa_selftest_exp2(xd.data_ptr(), poly.data_ptr(), sfu.data_ptr(), xd.numel()) == 0, lib.fa_selftest_error()
+    exact = torch.exp2(x.double())
+    fin = x >= -126.0
+    rel_poly = ((poly.cpu().double() - exact) / exact)[fin].abs().max().item()
+    big = x > -100.0  # ex2.approx.ftz flushes results below 2^-126
+    rel_sfu = ((sfu.cpu().double() - exact) / exact)[big].abs().max().item()
+    assert rel_poly < 4e-6, rel_poly
+    assert rel_sfu < 4e-6, rel_sfu
+    # exact powers of two and the masked entries
+    p = poly.cpu()
+    assert p[x == 0.0].eq(1.0).all() and p[x == 1.0].eq(2.0).all() and p[x == -1.0].eq(0.5).all()
+    assert (p[~fin] < 1e-37).all() and (p[~fin] >= 0).all()
+    assert (p[~fin].half() == 0).all()
