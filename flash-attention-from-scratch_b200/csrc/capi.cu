@@ -17,7 +17,6 @@
 
 #include "../../include/fa_b200.h"
 #include "fa_internal.h"
-#include "tma_host.h"
 
 namespace {
 
@@ -114,24 +113,26 @@ int launch_one(const FaFwdParams* p, cudaStream_t stream) {
         return cuda_fail(err, "cudaGetSymbolAddress");
     }
     const int bh = p->batch * p->heads;
-    CUtensorMap maps[4];
-    const void* ptrs[4] = {p->q, p->k, p->v, p->o};
-    for (int i = 0; i < 4; ++i) {
-        const CUresult cr =
-            fa_sm100::encode_bhnd_map(&maps[i], ptrs[i], bh, p->seqlen, p->head_dim, 128);
-        if (cr != CUDA_SUCCESS) {
-            return fail(FA_ERR_CUDA, "flash_fwd: cuTensorMapEncodeTiled failed (CUresult " +
-                                         std::to_string(static_cast<int>(cr)) + ")");
-        }
-    }
+    fa_sm100::FwdProblem prob{};
+    prob.q = p->q;
+    prob.k = p->k;
+    prob.v = p->v;
+    prob.o = p->o;
+    prob.num_bh = bh;
+    prob.seqlen = p->seqlen;
+    prob.head_dim = p->head_dim;
+    prob.causal = p->causal != 0;
+    prob.variant = p->variant;
     fa_sm100::FwdArgs args{};
     args.seqlen = p->seqlen;
     args.num_bh = bh;
     args.scale_log2 = static_cast<float>(static_cast<double>(p->softmax_scale) * M_LOG2E);
     args.epoch = next_epoch();
     args.status = status;
-    err = fa_sm100::launch_forward(p->head_dim, p->causal != 0, p->variant, maps[0], maps[1],
-                                   maps[2], maps[3], args, stream);
+    err = fa_sm100::launch_forward(prob, args, stream);
+    if (err == cudaErrorInvalidValue) {
+        return fail(FA_ERR_CUDA, "flash_fwd: cuTensorMapEncodeTiled failed");
+    }
     if (err != cudaSuccess) {
         return cuda_fail(err, "kernel launch");
     }

@@ -27,12 +27,23 @@ struct FwdArgs {
 // Variant ids as in the reference (csrc/flash_fwd.h:12-16).
 enum : int { kVariantBaseline = 0, kVariantOpt = 1, kVariantFp16Acc = 2 };
 
-// Launches the forward kernel for one (head_dim, causal, variant) on `stream`. The tensor
-// maps describe q, k, v, o as [B*H][N][D] fp16 with a 64 x 128 box and 128-byte swizzle.
-// Returns a cudaError_t.
-cudaError_t launch_forward(int head_dim, bool causal, int variant, const CUtensorMap& tm_q,
-                           const CUtensorMap& tm_k, const CUtensorMap& tm_v,
-                           const CUtensorMap& tm_o, const FwdArgs& args, cudaStream_t stream);
+// One forward problem: q, k, v, o are contiguous [B*H][N][D] fp16 device tensors.
+struct FwdProblem {
+    const void* q;
+    const void* k;
+    const void* v;
+    void* o;
+    int num_bh;
+    int seqlen;
+    int head_dim;
+    bool causal;
+    int variant;
+};
+
+// Encodes the TMA tensor maps the chosen kernel needs and launches it on `stream`.
+// Returns cudaSuccess, a CUDA launch error, or cudaErrorInvalidValue if a tensor map could not
+// be encoded.
+cudaError_t launch_forward(const FwdProblem& prob, const FwdArgs& args, cudaStream_t stream);
 
 // Shared-memory bytes and threads per CTA of a kernel instantiation (for reports / tests).
 int kernel_smem_bytes(int head_dim, bool causal, int variant);

@@ -40,14 +40,15 @@
 
 #include "fa_internal.h"
 #include "sm100_ptx.cuh"
+#include "tma_host.h"
 
 // Software-exp2 share (how many of every 8 column pairs of a 128-key tile take exp2_poly2
 // instead of ex2.approx); compile-time tuning knobs.
 #ifndef FA_EMU_PER8_D128
-#define FA_EMU_PER8_D128 2
+#define FA_EMU_PER8_D128 0
 #endif
 #ifndef FA_EMU_PER8_D64
-#define FA_EMU_PER8_D64 3
+#define FA_EMU_PER8_D64 2
 #endif
 // Register split between the softmax warpgroups and the producer/MMA warpgroup (NQ = 2):
 // 0 keeps every warp at the launch allocation (168); otherwise softmax warps go to this many
@@ -126,6 +127,28 @@ struct SharedBarriers {
     int abort;
 };
 
+// Optional event trace of one CTA (build with -DFA_TRACE; off in the product build): SM clock
+// stamps of the pipeline events of CTA (gridDim.x / 2, 0), read back with fa_trace_read().
+#ifdef FA_TRACE
+// [0, 2*4*64): softmax t (key tile j < 64): {S ready, S loaded, P stored + arrived, unused}
+// [1024, +2*4*64): MMA t: {P ready, PV issued, S(j+1) issued, V ready}
+// [2048, +256): producer ring slot: load issued
+__device__ unsigned long long g_fa_trace[4096];
+__device__ __forceinline__ bool trace_cta() {
+    return blockIdx.x == gridDim.x / 2 && blockIdx.y == 0;
+}
+#define FA_TRACE_AT(idx)                                      \
+    do {                                                      \
+        if (trace_cta()) {                                    \
+            g_fa_trace[(idx)] = clock64();                    \
+        }                                                     \
+    } while (0)
+#else
+#define FA_TRACE_AT(idx) \
+    do {                 \
+    } while (0)
+#endif
+
 __device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
 __device__ __forceinline__ uint32_t f2u(float x) { return __float_as_uint(x); }
 
@@ -134,41 +157,45 @@ __device__ __forceinline__ float f16cell_to_float(uint32_t cell) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(cell & 0xFFFFu)));
 }
 
+// MMA issue helpers. The issuing thread shares its SM sub-partition with busy softmax warps,
+// so descriptors are derived from precomputed bases with one add each (a descriptor's start
+// address is its low 14 bits in 16-byte units; shared memory stays below 256 KB, so adding an
+// offset never carries out of the field). `qd` = K-step descriptors of Q_t; `kd` / `vd` = the
+// descriptor of the K / V tile's first byte.
 template <class Cfg>
-__device__ __forceinline__ void issue_s_mma(uint32_t tmem_s, uint32_t q_addr, uint32_t k_addr) {
+__device__ __forceinline__ void issue_s_mma(uint32_t tmem_s, const uint64_t (&qd)[Cfg::D / 16],
+                                            uint64_t kd) {
     constexpr uint32_t idesc = make_idesc_f16(kBM, kBN, /*d_f32=*/true, /*b_mn_major=*/false);
 #pragma unroll
     for (int kk = 0; kk < Cfg::D / 16; ++kk) {
-        const uint32_t off = static_cast<uint32_t>((kk / 4) * kBoxBytes + (kk % 4) * 32);
-        umma_ss(tmem_s, make_desc_kmajor_sw128(q_addr + off), make_desc_kmajor_sw128(k_addr + off),
-                idesc, kk > 0 ? 1u : 0u);
+        const uint64_t off = static_cast<uint64_t>(((kk / 4) * kBoxBytes + (kk % 4) * 32) >> 4);
+        umma_ss(tmem_s, qd[kk], kd + off, idesc, kk > 0 ? 1u : 0u);
     }
 }
 
 // O (fp32) += P V over the 128 keys of one tile; `first` starts the accumulator.
 template <class Cfg>
-__device__ __forceinline__ void issue_pv_mma_f32(uint32_t tmem_o, uint32_t tmem_p, uint32_t v_addr,
+__device__ __forceinline__ void issue_pv_mma_f32(uint32_t tmem_o, uint32_t tmem_p, uint64_t vd,
                                                  bool first) {
     constexpr uint32_t idesc = make_idesc_f16(kBM, Cfg::D, /*d_f32=*/true, /*b_mn_major=*/true);
 #pragma unroll
     for (int kk = 0; kk < kBN / 16; ++kk) {
-        umma_ts(tmem_o, tmem_p + kk * 8, make_desc_mnmajor_sw128(v_addr + kk * 2048, kBoxBytes),
-                idesc, (first && kk == 0) ? 0u : 1u);
+        umma_ts(tmem_o, tmem_p + kk * 8, vd + static_cast<uint64_t>(kk * (2048 >> 4)), idesc,
+                (first && kk == 0) ? 0u : 1u);
     }
 }
 
 // fp16acc: T_h = P[:, 64h:64h+64] V[64h:64h+64, :] accumulated in fp16, fresh per tile.
 template <class Cfg>
-__device__ __forceinline__ void issue_pv_mma_f16(uint32_t tmem_t, uint32_t tmem_p, uint32_t v_addr) {
+__device__ __forceinline__ void issue_pv_mma_f16(uint32_t tmem_t, uint32_t tmem_p, uint64_t vd) {
     constexpr uint32_t idesc = make_idesc_f16(kBM, Cfg::D, /*d_f32=*/false, /*b_mn_major=*/true);
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
 #pragma unroll
         for (int k4 = 0; k4 < 4; ++k4) {
             const int kk = h * 4 + k4;
-            umma_ts(tmem_t + h * Cfg::D, tmem_p + kk * 8,
-                    make_desc_mnmajor_sw128(v_addr + kk * 2048, kBoxBytes), idesc,
-                    k4 == 0 ? 0u : 1u);
+            umma_ts(tmem_t + h * Cfg::D, tmem_p + kk * 8, vd + static_cast<uint64_t>(kk * (2048 >> 4)),
+                    idesc, k4 == 0 ? 0u : 1u);
         }
     }
 }
@@ -305,6 +332,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             if (!ok) {
                 break;
             }
+            if (row == 0 && j < 64) {
+                FA_TRACE_AT((t * 64 + j) * 4 + 0);
+            }
             tc_fence_after();
             uint32_t sr[kBN];
 #pragma unroll
@@ -312,6 +342,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 tmem_ld32(t_s + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
             }
             tmem_wait_ld();
+            if (row == 0 && j < 64) {
+                FA_TRACE_AT((t * 64 + j) * 4 + 1);
+            }
             if constexpr (Cfg::SEP_P) {
                 // S_t is in registers: the MMA warp may overwrite it with S_t(j+1).
                 tc_fence_before();
@@ -376,12 +409,13 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     uint32_t h;
                     if constexpr (Cfg::EXP16) {
                         h = ex2_approx_f16x2(pack_half2(x2.x, x2.y));
-                    } else if ((i % 8) < Cfg::kEmuPer8) {
-                        const float2 e = exp2_poly2(x2);
-                        h = pack_half2(e.x, e.y);
                     } else {
-                        h = pack_half2(ex2_approx(x2.x), ex2_approx(x2.y));
+                        const float2 e = ((i % 8) < Cfg::kEmuPer8)
+                                             ? exp2_poly2(x2)
+                                             : make_float2(ex2_approx(x2.x), ex2_approx(x2.y));
+                        h = pack_half2(e.x, e.y);
                     }
+                    // The row sum adds the fp16-rounded values the MMA consumes.
                     sum2[i % 4] = __fadd2_rn(sum2[i % 4], unpack_half2(h));
                     pk[i] = h;
                 }
@@ -412,6 +446,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(bar_p);
+                if (row == 0 && j < 64) {
+                    FA_TRACE_AT((t * 64 + j) * 4 + 2);
+                }
             } else {
                 tmem_wait_st();
                 tc_fence_before();
@@ -536,6 +573,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     }
                     loaded[stage] = true;
                     last_parity[stage] = phase;
+                    if (ring < 256) {
+                        FA_TRACE_AT(2048 + ring);
+                    }
                     ++ring;
                 }
             }
@@ -567,6 +607,20 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             }
             const uint32_t q_addr0 = smem_base + Cfg::kSmemQ;
             const uint32_t kv_addr0 = smem_base + Cfg::kSmemKV;
+            uint64_t qd[NQ][D / 16];
+#pragma unroll
+            for (int t = 0; t < NQ; ++t) {
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    qd[t][kk] = make_desc_kmajor_sw128(q_addr0 + t * Cfg::kTileBytes +
+                                                       (kk / 4) * kBoxBytes + (kk % 4) * 32);
+                }
+            }
+            const uint64_t kd0 = make_desc_kmajor_sw128(kv_addr0);
+            const uint64_t vd0 = make_desc_mnmajor_sw128(kv_addr0, kBoxBytes);
+            auto stage_off = [](int stage) -> uint64_t {
+                return static_cast<uint64_t>(stage * (Cfg::kTileBytes >> 4));
+            };
             int ring = 0;
             if (ok && n_max > 0) {
                 ok = mbar_wait(smem_u32(&sb.kv_full[0]), 0, wctx, kStatusTimeoutMma);
@@ -575,8 +629,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 #pragma unroll
                     for (int t = 0; t < NQ; ++t) {
                         if (n_kv[t] > 0) {
-                            issue_s_mma<Cfg>(tmem + Cfg::kTmemS + t * kBN,
-                                             q_addr0 + t * Cfg::kTileBytes, kv_addr0);
+                            issue_s_mma<Cfg>(tmem + Cfg::kTmemS + t * kBN, qd[t], kd0);
                             umma_commit(smem_u32(&sb.s_full[t]));
                         }
                     }
@@ -612,12 +665,14 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                                 break;
                             }
                             tc_fence_after();
-                            issue_s_mma<Cfg>(s_addr, q_addr0 + t * Cfg::kTileBytes,
-                                             kv_addr0 + ks * Cfg::kTileBytes);
+                            issue_s_mma<Cfg>(s_addr, qd[t], kd0 + stage_off(ks));
                             umma_commit(smem_u32(&sb.s_full[t]));
                         }
                     }
                     ok = mbar_wait(smem_u32(&sb.p_full[t]), j & 1, wctx, kStatusTimeoutMma);
+                    if (j < 64) {
+                        FA_TRACE_AT(1024 + (t * 64 + j) * 4 + 0);
+                    }
                     if (ok && !v_ready) {
                         ok = mbar_wait(smem_u32(&sb.kv_full[vs]), (v_slot / STAGES) & 1, wctx,
                                        kStatusTimeoutMma);
@@ -627,17 +682,19 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t v_addr = kv_addr0 + vs * Cfg::kTileBytes;
+                    const uint64_t vd = vd0 + stage_off(vs);
                     if constexpr (Cfg::ACC16) {
-                        issue_pv_mma_f16<Cfg>(tmem + Cfg::kTmemExtra, s_addr, v_addr);
+                        issue_pv_mma_f16<Cfg>(tmem + Cfg::kTmemExtra, s_addr, vd);
                     } else if constexpr (Cfg::SEP_P) {
                         issue_pv_mma_f32<Cfg>(tmem + Cfg::kTmemO + t * Cfg::D,
-                                              tmem + Cfg::kTmemExtra + t * 64, v_addr, j == 0);
+                                              tmem + Cfg::kTmemExtra + t * 64, vd, j == 0);
                     } else {
-                        issue_pv_mma_f32<Cfg>(tmem + Cfg::kTmemO + t * Cfg::D, s_addr, v_addr,
-                                              j == 0);
+                        issue_pv_mma_f32<Cfg>(tmem + Cfg::kTmemO + t * Cfg::D, s_addr, vd, j == 0);
                     }
                     umma_commit(smem_u32(&sb.o_done[t]));
+                    if (j < 64) {
+                        FA_TRACE_AT(1024 + (t * 64 + j) * 4 + 1);
+                    }
                     if constexpr (!Cfg::SEP_P) {
                         // S_t(j+1) reuses the columns P_t(j) was read from by the MMAs above.
                         if (next_s) {
@@ -650,9 +707,11 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                                 tc_fence_after();
                                 k_ready = true;
                             }
-                            issue_s_mma<Cfg>(s_addr, q_addr0 + t * Cfg::kTileBytes,
-                                             kv_addr0 + ks * Cfg::kTileBytes);
+                            issue_s_mma<Cfg>(s_addr, qd[t], kd0 + stage_off(ks));
                             umma_commit(smem_u32(&sb.s_full[t]));
+                            if (j < 64) {
+                                FA_TRACE_AT(1024 + (t * 64 + j) * 4 + 2);
+                            }
                         }
                     }
                 }
@@ -715,16 +774,26 @@ cudaError_t launch_variant(int variant, const CUtensorMap& tm_q, const CUtensorM
     }
 }
 
-cudaError_t launch_forward(int head_dim, bool causal, int variant, const CUtensorMap& tm_q,
-                           const CUtensorMap& tm_k, const CUtensorMap& tm_v,
-                           const CUtensorMap& tm_o, const FwdArgs& args, cudaStream_t stream) {
-    if (head_dim == 64) {
-        return causal ? launch_variant<64, true>(variant, tm_q, tm_k, tm_v, tm_o, args, stream)
-                      : launch_variant<64, false>(variant, tm_q, tm_k, tm_v, tm_o, args, stream);
+cudaError_t launch_forward(const FwdProblem& prob, const FwdArgs& args, cudaStream_t stream) {
+    // This kernel: 128-row boxes for Q, K, V and O.
+    CUtensorMap maps[4];
+    const void* ptrs[4] = {prob.q, prob.k, prob.v, prob.o};
+    for (int i = 0; i < 4; ++i) {
+        if (encode_bhnd_map(&maps[i], ptrs[i], prob.num_bh, prob.seqlen, prob.head_dim, kBM) !=
+            CUDA_SUCCESS) {
+            return cudaErrorInvalidValue;
+        }
     }
-    if (head_dim == 128) {
-        return causal ? launch_variant<128, true>(variant, tm_q, tm_k, tm_v, tm_o, args, stream)
-                      : launch_variant<128, false>(variant, tm_q, tm_k, tm_v, tm_o, args, stream);
+    const int variant = prob.variant;
+    if (prob.head_dim == 64) {
+        return prob.causal
+                   ? launch_variant<64, true>(variant, maps[0], maps[1], maps[2], maps[3], args, stream)
+                   : launch_variant<64, false>(variant, maps[0], maps[1], maps[2], maps[3], args, stream);
+    }
+    if (prob.head_dim == 128) {
+        return prob.causal
+                   ? launch_variant<128, true>(variant, maps[0], maps[1], maps[2], maps[3], args, stream)
+                   : launch_variant<128, false>(variant, maps[0], maps[1], maps[2], maps[3], args, stream);
     }
     return cudaErrorInvalidValue;
 }
@@ -761,4 +830,26 @@ int kernel_threads(int head_dim, bool /*causal*/, int variant) {
     return head_dim == 64 ? threads_for<64>(variant) : threads_for<128>(variant);
 }
 
+#ifdef FA_TRACE
+int trace_read(unsigned long long* out, int n) {
+    if (n > 4096) {
+        n = 4096;
+    }
+    return cudaMemcpyFromSymbol(out, g_fa_trace, sizeof(unsigned long long) * n) == cudaSuccess ? n : -1;
+}
+int trace_clear() {
+    static unsigned long long zero[4096] = {};
+    return cudaMemcpyToSymbol(g_fa_trace, zero, sizeof(zero)) == cudaSuccess ? 0 : -1;
+}
+#endif
+
 }  // namespace fa_sm100
+
+#ifdef FA_TRACE
+extern "C" __attribute__((visibility("default"))) int fa_trace_read(unsigned long long* out, int n) {
+    return fa_sm100::trace_read(out, n);
+}
+extern "C" __attribute__((visibility("default"))) int fa_trace_clear(void) {
+    return fa_sm100::trace_clear();
+}
+#endif
