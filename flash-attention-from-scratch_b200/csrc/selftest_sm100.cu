@@ -189,6 +189,29 @@ __global__ void exp2_probe_kernel(const float* __restrict__ x, float* __restrict
     }
 }
 
+// Watchdog probe: waits with the kernels' bounded wait (mbar_wait) on an mbarrier that no
+// thread ever arrives on. The wait must give up after kWaitTimeoutNs, record its code in the
+// status word and let the kernel return; flags[0] = 1 if the wait reported failure, flags[1]
+// = 1 once the kernel reached its end.
+__global__ void watchdog_probe_kernel(int* flags) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        mbar_init(smem_u32(&bar), 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    const WaitCtx w{&abort_flag, &g_probe_status.code, &g_probe_status.epoch_aborted, 7u};
+    const bool ok = mbar_wait(smem_u32(&bar), 0, w, kStatusTimeoutSoftmax);
+    const bool all_failed = __all_sync(0xffffffffu, !ok);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        flags[0] = all_failed ? 1 : 0;
+        flags[1] = 1;
+    }
+}
+
 thread_local std::string g_err;
 
 }  // namespace
@@ -265,6 +288,31 @@ __attribute__((visibility("default"))) int fa_selftest_exp2(const float* x, floa
         g_err = std::string("CUDA error: ") + cudaGetErrorString(err);
         return 3;
     }
+    return 0;
+}
+
+// Runs the watchdog probe on the current device (one CTA of 64 threads) and synchronises.
+// Writes the probe's status word (then clears it) to *code_out. Returns 0 on success.
+__attribute__((visibility("default"))) int fa_selftest_watchdog(int* flags, unsigned* code_out) {
+    using namespace fa_sm100;
+    watchdog_probe_kernel<<<1, 64>>>(flags);
+    cudaError_t err = cudaGetLastError();
+    if (err == cudaSuccess) {
+        err = cudaDeviceSynchronize();
+    }
+    DeviceStatus st{};
+    if (err == cudaSuccess) {
+        err = cudaMemcpyFromSymbol(&st, g_probe_status, sizeof(st));
+    }
+    if (err == cudaSuccess) {
+        const DeviceStatus zero{};
+        err = cudaMemcpyToSymbol(g_probe_status, &zero, sizeof(zero));
+    }
+    if (err != cudaSuccess) {
+        g_err = std::string("CUDA error: ") + cudaGetErrorString(err);
+        return 3;
+    }
+    *code_out = st.code;
     return 0;
 }
 

@@ -87,3 +87,30 @@ def test_exp2_implementations_error_bounds():
     assert p[x == 0.0].eq(1.0).all() and p[x == 1.0].eq(2.0).all() and p[x == -1.0].eq(0.5).all()
     assert (p[~fin] < 1e-37).all() and (p[~fin] >= 0).all()
     assert (p[~fin].half() == 0).all()
+
+
+def test_bounded_wait_times_out_without_fault():
+    """Failure detection on the GPU without a fault: the kernels' bounded mbarrier wait, on a
+    barrier nothing arrives on, gives up after its time limit (1 s), records its code in the
+    status word and returns; the CUDA context stays usable afterwards."""
+    import time
+
+    lib = ctypes.CDLL(str(LIB))
+    lib.fa_selftest_watchdog.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+    lib.fa_selftest_error.restype = ctypes.c_char_p
+    flags = torch.zeros(2, dtype=torch.int32, device="cuda")
+    code = ctypes.c_uint32(0)
+    t0 = time.time()
+    rc = lib.fa_selftest_watchdog(flags.data_ptr(), ctypes.byref(code))
+    elapsed = time.time() - t0
+    assert rc == 0, lib.fa_selftest_error()
+    assert flags.tolist() == [1, 1]
+    assert code.value == 1 << 2  # kStatusTimeoutSoftmax
+    assert 0.9 < elapsed < 30.0
+    # the context is still healthy: run the real kernel
+    import fa
+    from fa.synthetic import make_qkv
+
+    q, k, v = (t.cuda() for t in make_qkv(1, 1, 64, 64, seed=1))
+    assert torch.isfinite(fa.forward(q, k, v)).all()
+    assert fa._C.device_status(0, clear=True) == 0
