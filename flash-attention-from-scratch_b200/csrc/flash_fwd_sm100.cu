@@ -268,10 +268,12 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         for (int t = 0; t < NQ; ++t) {
             mbar_init(smem_u32(&sb.q_full[t]), 1);
             mbar_init(smem_u32(&sb.s_full[t]), 1);
-            mbar_init(smem_u32(&sb.s_free[t]), 128);
-            mbar_init(smem_u32(&sb.p_full[t]), 128);
+            // Softmax-side barriers take one arrival per warp (after __syncwarp), not one per
+            // thread: 128 arrivals on one barrier word serialise in the shared-memory atomics.
+            mbar_init(smem_u32(&sb.s_free[t]), 4);
+            mbar_init(smem_u32(&sb.p_full[t]), 4);
             mbar_init(smem_u32(&sb.o_done[t]), 1);
-            mbar_init(smem_u32(&sb.epi[t]), 128);
+            mbar_init(smem_u32(&sb.epi[t]), 4);
         }
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(smem_u32(&sb.kv_full[s]), 1);
@@ -348,7 +350,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             if constexpr (Cfg::SEP_P) {
                 // S_t is in registers: the MMA warp may overwrite it with S_t(j+1).
                 tc_fence_before();
-                mbar_arrive(bar_sf);
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(bar_sf);
+                }
             }
 
             const int kbase = j * kBN;
@@ -445,14 +450,20 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 }
                 tmem_wait_st();
                 tc_fence_before();
-                mbar_arrive(bar_p);
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(bar_p);
+                }
                 if (row == 0 && j < 64) {
                     FA_TRACE_AT((t * 64 + j) * 4 + 2);
                 }
             } else {
                 tmem_wait_st();
                 tc_fence_before();
-                mbar_arrive(bar_p);
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(bar_p);
+                }
                 // Fold this tile's two fp16 partials into the fp32 accumulator:
                 // O = alpha * O + T_0 + T_1.
                 ok = __all_sync(0xffffffffu, mbar_wait(bar_o, j & 1, wctx, kStatusTimeoutSoftmax));
@@ -516,7 +527,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 }
             }
             fence_proxy_async_smem();
-            mbar_arrive(smem_u32(&sb.epi[t]));
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(smem_u32(&sb.epi[t]));
+            }
             if (row == 0) {
                 if (mbar_wait(smem_u32(&sb.epi[t]), 0, wctx, kStatusTimeoutEpilogue)) {
 #pragma unroll
