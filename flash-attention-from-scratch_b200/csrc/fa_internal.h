@@ -22,6 +22,7 @@ struct FwdArgs {
     float scale_log2;     // softmax_scale * log2(e)
     unsigned epoch;       // launch epoch, never 0
     DeviceStatus* status; // per-device watchdog record
+    int head_group;       // causal schedule: heads interleaved in one heavy-first sweep (>= 1)
 };
 
 // Variant ids as in the reference (csrc/flash_fwd.h:12-16).

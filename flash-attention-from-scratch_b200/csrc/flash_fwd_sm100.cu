@@ -19,8 +19,10 @@
 //   warpgroup NQ        warp 0: TMA producer (Q tiles once, then K_0, V_0, K_1, V_1, ...
 //                       through a STAGES-deep ring of 128 x D tiles, 128-byte swizzle);
 //                       warp 1: MMA issuer (one thread) and TMEM allocation; warps 2-3 idle.
-//   With NQ = 2 the softmax warpgroups raise their register limit (setmaxnreg) with the
-//   registers the producer/MMA warpgroup gives up.
+//   Build options (measured on B200, off by default): FA_SPLIT_COLS=2 gives each query tile
+//   two softmax warpgroups that split its 128 key columns and exchange row maxima and sums
+//   through shared memory over a 64-thread named barrier; FA_REGS_SOFTMAX=R moves registers
+//   from the producer/MMA warpgroup to the softmax warpgroups (setmaxnreg).
 //
 // Tensor memory (512 columns x 128 lanes, fp32 cells):
 //   S_t  columns [128 t, 128 t + 128)   scores of tile t, fp32
@@ -36,6 +38,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 
 #include "fa_internal.h"
@@ -55,6 +58,12 @@
 // and the other warpgroup gives up the difference.
 #ifndef FA_REGS_SOFTMAX
 #define FA_REGS_SOFTMAX 0
+#endif
+// Softmax warpgroups per query tile (fp32 variants): 2 splits the 128 columns of S between two
+// warpgroups that own the same rows and exchange row maxima through shared memory. Measured on
+// B200 at d = 128: no faster than 1 (the exponentials, not the warps' latency, bound a tile).
+#ifndef FA_SPLIT_COLS
+#define FA_SPLIT_COLS 1
 #endif
 
 namespace fa_sm100 {
@@ -93,24 +102,38 @@ struct FwdCfg {
     static constexpr int kTmemUsed = kTmemExtra + (ACC16 ? 2 * D : (SEP_P ? NQ * 64 : 0));
     static constexpr int kTmemCols = 512;
     static_assert(kTmemUsed <= kTmemCols, "tensor memory budget");
-    // Warps: NQ softmax warpgroups + one producer/MMA warpgroup.
-    static constexpr int kSoftmaxWarps = 4 * NQ;
+    // Warps: NQ x SPLIT softmax warpgroups + one producer/MMA warpgroup. With SPLIT = 2 the
+    // warpgroup (t, h) owns rows 0..127 of query tile t and S columns [64 h, 64 h + 64).
+    static constexpr int SPLIT = ACC16 ? 1 : FA_SPLIT_COLS;
+    static constexpr int kCols = kBN / SPLIT;  // S columns per softmax thread
+    static constexpr int kSoftmaxWarps = 4 * NQ * SPLIT;
     static constexpr int kProducerWarp = kSoftmaxWarps;
     static constexpr int kMmaWarp = kSoftmaxWarps + 1;
     static constexpr int kThreads = 32 * (kSoftmaxWarps + 4);
-    // Register split (NQ = 2, 384 threads launched at 168 each): softmax warpgroups to
-    // kRegsSoftmax, the producer/MMA warpgroup to what is left (multiple of 8).
-    static constexpr int kRegsLaunch = 168;
+    // Register split: every warp is launched with kRegsLaunch (65536 / threads, a multiple of
+    // 8); with FA_REGS_SOFTMAX != 0 the softmax warpgroups go to that many and the
+    // producer/MMA warpgroup gives up the difference.
+    static constexpr int kRegsLaunch = ((65536 / kThreads) / 8 * 8) > 255 ? 248 : (65536 / kThreads) / 8 * 8;
     static constexpr int kRegsSoftmax = FA_REGS_SOFTMAX;
     static constexpr int kRegsOther =
-        kRegsSoftmax == 0 ? kRegsLaunch : ((kThreads * kRegsLaunch - 256 * kRegsSoftmax) / 128) / 8 * 8;
+        kRegsSoftmax == 0
+            ? kRegsLaunch
+            : ((kThreads * kRegsLaunch - 32 * kSoftmaxWarps * kRegsSoftmax) / 128) / 8 * 8;
     static_assert(kRegsSoftmax == 0 || NQ != 2 ||
-                      (256 * kRegsSoftmax + 128 * kRegsOther <= kThreads * kRegsLaunch &&
+                      (32 * kSoftmaxWarps * kRegsSoftmax + 128 * kRegsOther <= kThreads * kRegsLaunch &&
                        kRegsOther >= 24 && kRegsSoftmax % 8 == 0 && kRegsSoftmax <= 256),
                   "register split exceeds the launch allocation");
+    static_assert(SPLIT == 1 || SPLIT == 2, "column split");
     static_assert(D == 64 || D == 128, "head dim");
     static_assert(kSmemAlloc <= 227 * 1024, "shared memory budget");
     static_assert(kSmemAlloc > 114 * 1024, "one CTA per SM (it owns all 512 TMEM columns)");
+};
+
+// Row statistics exchanged between the two column halves of a query tile (SPLIT = 2):
+// red_max[j % 2][t][h][row] per key tile, red_sum[t][h][row] once at the end.
+struct SharedRowStats {
+    float red_max[2][2][2][128];
+    float red_sum[2][2][128];
 };
 
 struct SharedBarriers {
@@ -130,7 +153,7 @@ struct SharedBarriers {
 // Optional event trace of one CTA (build with -DFA_TRACE; off in the product build): SM clock
 // stamps of the pipeline events of CTA (gridDim.x / 2, 0), read back with fa_trace_read().
 #ifdef FA_TRACE
-// [0, 2*4*64): softmax t (key tile j < 64): {S ready, S loaded, P stored + arrived, unused}
+// [0, 2*4*64): softmax t (key tile j < 64): {S ready, S loaded, P stored + arrived, row max}
 // [1024, +2*4*64): MMA t: {P ready, PV issued, S(j+1) issued, V ready}
 // [2048, +256): producer ring slot: load issued
 __device__ unsigned long long g_fa_trace[4096];
@@ -160,16 +183,15 @@ __device__ __forceinline__ float f16cell_to_float(uint32_t cell) {
 // MMA issue helpers. The issuing thread shares its SM sub-partition with busy softmax warps,
 // so descriptors are derived from precomputed bases with one add each (a descriptor's start
 // address is its low 14 bits in 16-byte units; shared memory stays below 256 KB, so adding an
-// offset never carries out of the field). `qd` = K-step descriptors of Q_t; `kd` / `vd` = the
-// descriptor of the K / V tile's first byte.
+// offset never carries out of the field). `qd` / `kd` / `vd` = the descriptor of the Q / K / V
+// tile's first byte.
 template <class Cfg>
-__device__ __forceinline__ void issue_s_mma(uint32_t tmem_s, const uint64_t (&qd)[Cfg::D / 16],
-                                            uint64_t kd) {
+__device__ __forceinline__ void issue_s_mma(uint32_t tmem_s, uint64_t qd, uint64_t kd) {
     constexpr uint32_t idesc = make_idesc_f16(kBM, kBN, /*d_f32=*/true, /*b_mn_major=*/false);
 #pragma unroll
     for (int kk = 0; kk < Cfg::D / 16; ++kk) {
         const uint64_t off = static_cast<uint64_t>(((kk / 4) * kBoxBytes + (kk % 4) * 32) >> 4);
-        umma_ss(tmem_s, qd[kk], kd + off, idesc, kk > 0 ? 1u : 0u);
+        umma_ss(tmem_s, qd + off, kd + off, idesc, kk > 0 ? 1u : 0u);
     }
 }
 
@@ -200,18 +222,18 @@ __device__ __forceinline__ void issue_pv_mma_f16(uint32_t tmem_t, uint32_t tmem_
     }
 }
 
-// Row max (or min, for a negative scale) of 128 scores: eight independent three-input chains.
-template <bool MAX>
-__device__ __forceinline__ float row_extreme(const uint32_t (&sr)[kBN]) {
+// Row max (or min, for a negative scale) of N scores (N = 64 or 128): eight independent
+// three-input chains over columns 8 .. N-9, then the last eight columns.
+template <bool MAX, int N>
+__device__ __forceinline__ float row_extreme(const uint32_t (&sr)[N]) {
+    static_assert(N % 16 == 0 && N >= 32, "row_extreme covers N = 16 k columns");
     float m[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         m[i] = u2f(sr[i]);
     }
-    // Columns 8 .. 119 two groups of 8 at a time, then 120 .. 127.
-    static_assert(kBN == 128, "the reduction below is written for 128 columns");
 #pragma unroll
-    for (int c = 8; c + 16 <= kBN; c += 16) {
+    for (int c = 8; c + 16 <= N; c += 16) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             m[i] = MAX ? fmax3(m[i], u2f(sr[c + i]), u2f(sr[c + 8 + i]))
@@ -220,10 +242,15 @@ __device__ __forceinline__ float row_extreme(const uint32_t (&sr)[kBN]) {
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        m[i] = MAX ? fmaxf(m[i], u2f(sr[kBN - 8 + i])) : fminf(m[i], u2f(sr[kBN - 8 + i]));
+        m[i] = MAX ? fmaxf(m[i], u2f(sr[N - 8 + i])) : fminf(m[i], u2f(sr[N - 8 + i]));
     }
     return MAX ? fmax3(fmax3(m[0], m[1], m[2]), fmax3(m[3], m[4], m[5]), fmaxf(m[6], m[7]))
                : fmin3(fmin3(m[0], m[1], m[2]), fmin3(m[3], m[4], m[5]), fminf(m[6], m[7]));
+}
+
+// Named barrier over the two warps (one per column half) that own the same 32 rows.
+__device__ __forceinline__ void pair_sync(int id) {
+    asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
 }
 
 template <class Cfg>
@@ -238,6 +265,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 
     extern __shared__ uint8_t smem_raw[];
     __shared__ SharedBarriers sb;
+    __shared__ SharedRowStats rs;
 
     const int warp = static_cast<int>(threadIdx.x) / 32;
     const int lane = static_cast<int>(threadIdx.x) % 32;
@@ -246,10 +274,23 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     const uint32_t smem_base = smem_u32(smem);
 
     const int n = args.seqlen;
-    const int bh = static_cast<int>(blockIdx.y);
-    // Causal: block x covers more key tiles the later its rows are; launch the longest first.
-    const int m_block = Cfg::CAUSAL ? static_cast<int>(gridDim.x - 1 - blockIdx.x)
-                                    : static_cast<int>(blockIdx.x);
+    int bh = static_cast<int>(blockIdx.y);
+    int m_block = static_cast<int>(blockIdx.x);
+    if constexpr (Cfg::CAUSAL) {
+        // A causal row block covers more key tiles the later its rows are. CTAs start in
+        // linear-id order, so the linear id is mapped to (row block, head) longest first across
+        // a group of args.head_group heads (whose K/V stay resident in L2 together): the short
+        // blocks of every group then fill the gaps the long ones leave, instead of a head's
+        // long block starting last and running alone.
+        const int nb = static_cast<int>(gridDim.x);
+        const int lin = static_cast<int>(blockIdx.x) + nb * static_cast<int>(blockIdx.y);
+        const int group = lin / (nb * args.head_group);
+        const int head0 = group * args.head_group;
+        const int heads = min(args.head_group, args.num_bh - head0);
+        const int within = lin - group * nb * args.head_group;
+        bh = head0 + within % heads;
+        m_block = nb - 1 - within / heads;
+    }
     const int q_row0 = m_block * NQ * kBM;
     const int n_tiles_all = (n + kBN - 1) / kBN;
     int n_kv[NQ];
@@ -270,10 +311,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             mbar_init(smem_u32(&sb.s_full[t]), 1);
             // Softmax-side barriers take one arrival per warp (after __syncwarp), not one per
             // thread: 128 arrivals on one barrier word serialise in the shared-memory atomics.
-            mbar_init(smem_u32(&sb.s_free[t]), 4);
-            mbar_init(smem_u32(&sb.p_full[t]), 4);
+            mbar_init(smem_u32(&sb.s_free[t]), 4 * Cfg::SPLIT);
+            mbar_init(smem_u32(&sb.p_full[t]), 4 * Cfg::SPLIT);
             mbar_init(smem_u32(&sb.o_done[t]), 1);
-            mbar_init(smem_u32(&sb.epi[t]), 4);
+            mbar_init(smem_u32(&sb.epi[t]), 4 * Cfg::SPLIT);
         }
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(smem_u32(&sb.kv_full[s]), 1);
@@ -307,14 +348,21 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 
     if (warp < Cfg::kSoftmaxWarps) {
         // ================================ softmax warpgroups ================================
-        const int t = warp / 4;
-        const int row = (warp % 4) * 32 + lane;  // TMEM lane == query row within the tile
+        constexpr int SPLIT = Cfg::SPLIT;
+        constexpr int NC = Cfg::kCols;                 // S columns of this thread
+        const int t = (warp / 4) % NQ;                  // query tile
+        const int half = warp / (4 * NQ);               // column half (0 when SPLIT == 1)
+        const int row = (warp % 4) * 32 + lane;         // TMEM lane == query row within the tile
+        const int col0 = half * NC;                     // first S column of this thread
         const int q0 = q_row0 + t * kBM;
-        const int grow = q0 + row;                // global query row
+        const int grow = q0 + row;                      // global query row
+        const int pair_id = 1 + t * 4 + (warp % 4);     // named barrier of the two halves
         const uint32_t lane_off = static_cast<uint32_t>((warp % 4) * 32) << 16;
-        const uint32_t t_s = tmem + lane_off + Cfg::kTmemS + t * kBN;
-        const uint32_t t_o = tmem + lane_off + Cfg::kTmemO + t * D;
-        const uint32_t t_p = Cfg::SEP_P ? (tmem + lane_off + Cfg::kTmemExtra + t * 64) : t_s;
+        const uint32_t t_s = tmem + lane_off + Cfg::kTmemS + t * kBN + col0;
+        constexpr int OC = D / SPLIT;                   // O columns this thread rescales / stores
+        const uint32_t t_o = tmem + lane_off + Cfg::kTmemO + t * D + half * OC;
+        const uint32_t t_p = (Cfg::SEP_P ? (tmem + lane_off + Cfg::kTmemExtra + t * 64)
+                                         : (tmem + lane_off + Cfg::kTmemS + t * kBN)) + col0 / 2;
         const uint32_t t_t = tmem + lane_off + Cfg::kTmemExtra;
         const uint32_t bar_s = smem_u32(&sb.s_full[t]);
         const uint32_t bar_sf = smem_u32(&sb.s_free[t]);
@@ -326,25 +374,30 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         const int lim = Cfg::CAUSAL ? min(n - 1, grow) : (n - 1);
 
         float row_max = -INFINITY;  // running max of the scaled scores (log2 units)
-        float row_sum = 0.0f;       // running sum of the fp16-rounded probabilities
+        float row_sum = 0.0f;       // running sum of this thread's fp16-rounded probabilities
         bool ok = true;
 
+        // A warp that gave up on a wait keeps iterating without touching TMEM, so that the two
+        // column halves of a row always pass the same number of pair barriers.
         for (int j = 0; j < nt; ++j) {
-            ok = __all_sync(0xffffffffu, mbar_wait(bar_s, j & 1, wctx, kStatusTimeoutSoftmax));
+            ok = ok && __all_sync(0xffffffffu, mbar_wait(bar_s, j & 1, wctx, kStatusTimeoutSoftmax));
             if (!ok) {
-                break;
+                if constexpr (SPLIT == 2) {
+                    pair_sync(pair_id);
+                }
+                continue;
             }
-            if (row == 0 && j < 64) {
+            if (row == 0 && half == 0 && j < 64) {
                 FA_TRACE_AT((t * 64 + j) * 4 + 0);
             }
             tc_fence_after();
-            uint32_t sr[kBN];
+            uint32_t sr[NC];
 #pragma unroll
-            for (int c = 0; c < kBN / 32; ++c) {
+            for (int c = 0; c < NC / 32; ++c) {
                 tmem_ld32(t_s + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
             }
             tmem_wait_ld();
-            if (row == 0 && j < 64) {
+            if (row == 0 && half == 0 && j < 64) {
                 FA_TRACE_AT((t * 64 + j) * 4 + 1);
             }
             if constexpr (Cfg::SEP_P) {
@@ -364,19 +417,33 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             float mul;
             if (masked) {
                 // Scale first, then mask, so masked scores are -inf whatever the scale's sign.
-                const int cmax = lim - kbase;
+                const int cmax = lim - kbase - col0;
 #pragma unroll
-                for (int c = 0; c < kBN; ++c) {
+                for (int c = 0; c < NC; ++c) {
                     sr[c] = f2u((c > cmax) ? -INFINITY : u2f(sr[c]) * scale_log2);
                 }
-                tile_max = row_extreme<true>(sr);
+                tile_max = row_extreme<true, NC>(sr);
                 mul = 1.0f;
             } else {
-                tile_max = (scale_log2 >= 0.0f ? row_extreme<true>(sr) : row_extreme<false>(sr)) *
+                // max(s * scale) is max(s) * scale, or min(s) * scale for a negative scale.
+                tile_max = (scale_log2 >= 0.0f ? row_extreme<true, NC>(sr)
+                                               : row_extreme<false, NC>(sr)) *
                            scale_log2;
                 mul = scale_log2;
             }
+            if constexpr (SPLIT == 2) {
+                // Row max over both column halves (one buffer per key-tile parity, so a half
+                // that runs ahead never overwrites a value its partner has yet to read). A
+                // partner that aborted meets this barrier from its own branch above; the value
+                // read is then stale, and the abort flag stops this warp at its next wait.
+                rs.red_max[j & 1][t][half][row] = tile_max;
+                pair_sync(pair_id);
+                tile_max = fmaxf(tile_max, rs.red_max[j & 1][t][half ^ 1][row]);
+            }
 
+            if (row == 0 && half == 0 && j < 64) {
+                FA_TRACE_AT((t * 64 + j) * 4 + 3);
+            }
             // Running max update (lazy for "opt": keep the old max unless it grew by > 2^8).
             const float new_max = (tile_max > row_max + Cfg::kRescaleThreshold) ? tile_max : row_max;
             const float max_used = (new_max == -INFINITY) ? 0.0f : new_max;
@@ -391,7 +458,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 ok = __all_sync(0xffffffffu,
                                 mbar_wait(bar_o, (j - 1) & 1, wctx, kStatusTimeoutSoftmax));
                 if (!ok) {
-                    break;
+                    continue;
                 }
                 tc_fence_after();
             }
@@ -405,11 +472,11 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 sum2[i] = make_float2(0.0f, 0.0f);
             }
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
+            for (int chunk = 0; chunk < NC / 64; ++chunk) {
                 uint32_t pk[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
-                    const int c = half * 64 + 2 * i;
+                    const int c = chunk * 64 + 2 * i;
                     const float2 x2 = __ffma2_rn(make_float2(u2f(sr[c]), u2f(sr[c + 1])), mul2, neg2);
                     uint32_t h;
                     if constexpr (Cfg::EXP16) {
@@ -424,7 +491,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     sum2[i % 4] = __fadd2_rn(sum2[i % 4], unpack_half2(h));
                     pk[i] = h;
                 }
-                tmem_st32(t_p + half * 32, pk);
+                tmem_st32(t_p + chunk * 32, pk);
             }
             const float2 s01 = __fadd2_rn(sum2[0], sum2[1]);
             const float2 s23 = __fadd2_rn(sum2[2], sum2[3]);
@@ -435,7 +502,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 if (need_rescale) {
                     const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll
-                    for (int c = 0; c < D / 32; ++c) {
+                    for (int c = 0; c < OC / 32; ++c) {
                         uint32_t o[32];
                         tmem_ld32(t_o + c * 32, o);
                         tmem_wait_ld();
@@ -454,7 +521,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 if (lane == 0) {
                     mbar_arrive(bar_p);
                 }
-                if (row == 0 && j < 64) {
+                if (row == 0 && half == 0 && j < 64) {
                     FA_TRACE_AT((t * 64 + j) * 4 + 2);
                 }
             } else {
@@ -468,7 +535,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 // O = alpha * O + T_0 + T_1.
                 ok = __all_sync(0xffffffffu, mbar_wait(bar_o, j & 1, wctx, kStatusTimeoutSoftmax));
                 if (!ok) {
-                    break;
+                    continue;
                 }
                 tc_fence_after();
 #pragma unroll
@@ -501,13 +568,21 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 tc_fence_after();
             }
         }
+        if constexpr (SPLIT == 2) {
+            // Row sum over both column halves. Both warps of the pair reach this barrier: they
+            // share every loop decision above (same waits, votes and maxima), so either both
+            // are here with ok, or both aborted at the same step.
+            rs.red_sum[t][half][row] = row_sum;
+            pair_sync(pair_id);
+            row_sum += rs.red_sum[t][half ^ 1][row];
+        }
         if (ok && nt > 0) {
             const float inv_sum = (row_sum > 0.0f) ? (1.0f / row_sum) : 0.0f;
             // Stage O (fp16) in this tile's Q buffer, in the swizzled layout of the TMA box.
             // Every MMA that read Q_t has completed (its S was consumed above).
             uint8_t* out = smem + Cfg::kSmemQ + t * Cfg::kTileBytes;
 #pragma unroll
-            for (int c = 0; c < D / 32; ++c) {
+            for (int c = 0; c < OC / 32; ++c) {
                 uint32_t o[32];
                 tmem_ld32(t_o + c * 32, o);
                 tmem_wait_ld();
@@ -516,8 +591,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 for (int e = 0; e < 16; ++e) {
                     h[e] = pack_half2(u2f(o[2 * e]) * inv_sum, u2f(o[2 * e + 1]) * inv_sum);
                 }
-                const int box = (c * 32) / 64;
-                const int chunk0 = ((c * 32) % 64) / 8;
+                const int col = half * OC + c * 32;  // first O column of this chunk
+                const int box = col / 64;
+                const int chunk0 = (col % 64) / 8;
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const int cc = chunk0 + i;
@@ -531,7 +607,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             if (lane == 0) {
                 mbar_arrive(smem_u32(&sb.epi[t]));
             }
-            if (row == 0) {
+            if (row == 0 && half == 0) {
                 if (mbar_wait(smem_u32(&sb.epi[t]), 0, wctx, kStatusTimeoutEpilogue)) {
 #pragma unroll
                     for (int b = 0; b < Cfg::kBoxes; ++b) {
@@ -621,15 +697,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             }
             const uint32_t q_addr0 = smem_base + Cfg::kSmemQ;
             const uint32_t kv_addr0 = smem_base + Cfg::kSmemKV;
-            uint64_t qd[NQ][D / 16];
-#pragma unroll
-            for (int t = 0; t < NQ; ++t) {
-#pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk) {
-                    qd[t][kk] = make_desc_kmajor_sw128(q_addr0 + t * Cfg::kTileBytes +
-                                                       (kk / 4) * kBoxBytes + (kk % 4) * 32);
-                }
-            }
+            const uint64_t qd0 = make_desc_kmajor_sw128(q_addr0);
+            auto q_desc = [qd0](int t) -> uint64_t {
+                return qd0 + static_cast<uint64_t>(t * (Cfg::kTileBytes >> 4));
+            };
             const uint64_t kd0 = make_desc_kmajor_sw128(kv_addr0);
             const uint64_t vd0 = make_desc_mnmajor_sw128(kv_addr0, kBoxBytes);
             auto stage_off = [](int stage) -> uint64_t {
@@ -643,7 +714,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 #pragma unroll
                     for (int t = 0; t < NQ; ++t) {
                         if (n_kv[t] > 0) {
-                            issue_s_mma<Cfg>(tmem + Cfg::kTmemS + t * kBN, qd[t], kd0);
+                            issue_s_mma<Cfg>(tmem + Cfg::kTmemS + t * kBN, q_desc(t), kd0);
                             umma_commit(smem_u32(&sb.s_full[t]));
                         }
                     }
@@ -679,7 +750,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                                 break;
                             }
                             tc_fence_after();
-                            issue_s_mma<Cfg>(s_addr, qd[t], kd0 + stage_off(ks));
+                            issue_s_mma<Cfg>(s_addr, q_desc(t), kd0 + stage_off(ks));
                             umma_commit(smem_u32(&sb.s_full[t]));
                         }
                     }
@@ -721,7 +792,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                                 tc_fence_after();
                                 k_ready = true;
                             }
-                            issue_s_mma<Cfg>(s_addr, qd[t], kd0 + stage_off(ks));
+                            issue_s_mma<Cfg>(s_addr, q_desc(t), kd0 + stage_off(ks));
                             umma_commit(smem_u32(&sb.s_full[t]));
                             if (j < 64) {
                                 FA_TRACE_AT(1024 + (t * 64 + j) * 4 + 2);
@@ -766,9 +837,15 @@ cudaError_t launch_cfg(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const C
         return err;
     }
     const int rows_per_cta = Cfg::NQ * kBM;
+    // Heads per heavy-first sweep of the causal schedule: as many as keep their K and V
+    // (2 * N * D * 2 bytes each) within about 48 MiB of the 126 MB L2.
+    FwdArgs launch_args = args;
+    const double kv_bytes = 4.0 * static_cast<double>(args.seqlen) * D;
+    launch_args.head_group =
+        static_cast<int>(std::min<double>(args.num_bh, std::max(1.0, (48.0 * 1048576.0) / kv_bytes)));
     const dim3 grid(static_cast<unsigned>((args.seqlen + rows_per_cta - 1) / rows_per_cta),
                     static_cast<unsigned>(args.num_bh));
-    kernel<<<grid, Cfg::kThreads, Cfg::kSmemAlloc, stream>>>(tm_q, tm_k, tm_v, tm_o, args);
+    kernel<<<grid, Cfg::kThreads, Cfg::kSmemAlloc, stream>>>(tm_q, tm_k, tm_v, tm_o, launch_args);
     return cudaGetLastError();
 }
 
