@@ -18,7 +18,9 @@
 //                       epilogue of its tile.
 //   warpgroup NQ        warp 0: TMA producer (Q tiles once, then K_0, V_0, K_1, V_1, ...
 //                       through a STAGES-deep ring of 128 x D tiles, 128-byte swizzle);
-//                       warp 1: MMA issuer (one thread) and TMEM allocation; warps 2-3 idle.
+//                       warp 1: MMA issuer (one thread) and TMEM allocation; warp 2: the
+//                       issuer of query tile 1 where tiles have their own issuers (d = 64);
+//                       the remaining warps idle.
 //   Build options (measured on B200, off by default): FA_SPLIT_COLS=2 gives each query tile
 //   two softmax warpgroups that split its 128 key columns and exchange row maxima and sums
 //   through shared memory over a 64-thread named barrier; FA_REGS_SOFTMAX=R moves registers
@@ -62,6 +64,20 @@
 // Softmax warpgroups per query tile (fp32 variants): 2 splits the 128 columns of S between two
 // warpgroups that own the same rows and exchange row maxima through shared memory. Measured on
 // B200 at d = 128: no faster than 1 (the exponentials, not the warps' latency, bound a tile).
+#ifndef FA_EXP_POLY_DEG
+#define FA_EXP_POLY_DEG 4
+#endif
+// MMA issuing threads per head dim (fp32 variants, NQ = 2): 2 gives each query tile its own
+// issuer warp, so the tensor pipe can interleave the two tiles' P.V / S MMAs. Measured on
+// B200: +5% at d = 64; at d = 128 the two tiles then fall into step (both softmaxes at once,
+// then both tiles' MMAs) and lose a quarter, so d = 128 keeps the single issuer, whose issue
+// order keeps the tiles alternating.
+#ifndef FA_MMA_ISSUERS_D64
+#define FA_MMA_ISSUERS_D64 2
+#endif
+#ifndef FA_MMA_ISSUERS_D128
+#define FA_MMA_ISSUERS_D128 1
+#endif
 #ifndef FA_SPLIT_COLS
 #define FA_SPLIT_COLS 1
 #endif
@@ -109,6 +125,8 @@ struct FwdCfg {
     static constexpr int kSoftmaxWarps = 4 * NQ * SPLIT;
     static constexpr int kProducerWarp = kSoftmaxWarps;
     static constexpr int kMmaWarp = kSoftmaxWarps + 1;
+    static constexpr int kIssuers =  // MMA issuer warps kMmaWarp + i
+        (NQ == 2 && (D == 64 ? FA_MMA_ISSUERS_D64 : FA_MMA_ISSUERS_D128) == 2) ? 2 : 1;
     static constexpr int kThreads = 32 * (kSoftmaxWarps + 4);
     // Register split: every warp is launched with kRegsLaunch (65536 / threads, a multiple of
     // 8); with FA_REGS_SOFTMAX != 0 the softmax warpgroups go to that many and the
@@ -156,6 +174,7 @@ struct SharedBarriers {
 // [0, 2*4*64): softmax t (key tile j < 64): {S ready, S loaded, P stored + arrived, row max}
 // [1024, +2*4*64): MMA t: {P ready, PV issued, S(j+1) issued, V ready}
 // [2048, +256): producer ring slot: load issued
+// [2304, +2*4*64): softmax t, key tile j: arrival on P-ready of each of the tile's four warps
 __device__ unsigned long long g_fa_trace[4096];
 __device__ __forceinline__ bool trace_cta() {
     return blockIdx.x == gridDim.x / 2 && blockIdx.y == 0;
@@ -318,9 +337,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         }
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(smem_u32(&sb.kv_full[s]), 1);
-            mbar_init(smem_u32(&sb.kv_empty[s]), 1);
+            mbar_init(smem_u32(&sb.kv_empty[s]), Cfg::kIssuers);
         }
-        mbar_init(smem_u32(&sb.mma_idle), 1);
+        mbar_init(smem_u32(&sb.mma_idle), Cfg::kIssuers);
         mbar_fence_init();
     }
     if (warp == Cfg::kMmaWarp) {
@@ -482,12 +501,21 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     if constexpr (Cfg::EXP16) {
                         h = ex2_approx_f16x2(pack_half2(x2.x, x2.y));
                     } else {
+#if FA_EXP_POLY_DEG == 3
+                        const float2 e = ((i % 8) < Cfg::kEmuPer8)
+                                             ? exp2_poly2_deg3(x2)
+                                             : make_float2(ex2_approx(x2.x), ex2_approx(x2.y));
+#else
                         const float2 e = ((i % 8) < Cfg::kEmuPer8)
                                              ? exp2_poly2(x2)
                                              : make_float2(ex2_approx(x2.x), ex2_approx(x2.y));
+#endif
                         h = pack_half2(e.x, e.y);
                     }
-                    // The row sum adds the fp16-rounded values the MMA consumes.
+                    // The row sum adds the fp16-rounded values the MMA consumes, so that O is
+                    // normalised by the weights it was accumulated with. (The reference sums
+                    // the fp32 values, csrc/kernels/flash_fwd.cu:403-417; measured here that
+                    // is ~6% faster per tile but adds error: cfg4's outlier rows exceed 2e-3.)
                     sum2[i % 4] = __fadd2_rn(sum2[i % 4], unpack_half2(h));
                     pk[i] = h;
                 }
@@ -520,6 +548,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 __syncwarp();
                 if (lane == 0) {
                     mbar_arrive(bar_p);
+                    if (half == 0 && j < 64) {
+                        FA_TRACE_AT(2304 + (t * 64 + j) * 4 + (warp % 4));
+                    }
                 }
                 if (row == 0 && half == 0 && j < 64) {
                     FA_TRACE_AT((t * 64 + j) * 4 + 2);
@@ -685,7 +716,121 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             }
         }
         __syncwarp();
-    } else if (warp == Cfg::kMmaWarp) {
+    } else if (Cfg::kIssuers == 2 && warp >= Cfg::kMmaWarp && warp < Cfg::kMmaWarp + 2) {
+        // =========================== MMA issuers, one per query tile ===========================
+        // Issuer t walks the whole K/V ring (so that each slot's release takes one arrival per
+        // issuer) and issues only tile t's MMAs. It waits for every slot to land before it
+        // releases it, even one its tile does not read, so it can never release a later use
+        // of a slot before the producer has filled the current one.
+        if (lane == 0) {
+            const int t = warp - Cfg::kMmaWarp;
+            bool ok = true;
+            if (n_kv[t] > 0) {
+                ok = mbar_wait(smem_u32(&sb.q_full[t]), 0, wctx, kStatusTimeoutMma);
+            }
+            const uint32_t kv_addr0 = smem_base + Cfg::kSmemKV;
+            const uint64_t qd = make_desc_kmajor_sw128(smem_base + Cfg::kSmemQ + t * Cfg::kTileBytes);
+            const uint64_t kd0 = make_desc_kmajor_sw128(kv_addr0);
+            const uint64_t vd0 = make_desc_mnmajor_sw128(kv_addr0, kBoxBytes);
+            auto stage_off = [](int stage) -> uint64_t {
+                return static_cast<uint64_t>(stage * (Cfg::kTileBytes >> 4));
+            };
+            const uint32_t s_addr = tmem + Cfg::kTmemS + t * kBN;
+            const uint32_t o_addr = tmem + Cfg::kTmemO + t * Cfg::D;
+            const uint32_t p_addr = Cfg::SEP_P ? (tmem + Cfg::kTmemExtra + t * 64) : s_addr;
+            int ring = 0;
+            if (ok && n_max > 0) {
+                ok = mbar_wait(smem_u32(&sb.kv_full[0]), 0, wctx, kStatusTimeoutMma);
+                if (ok) {
+                    tc_fence_after();
+                    if (n_kv[t] > 0) {
+                        issue_s_mma<Cfg>(s_addr, qd, kd0);
+                        umma_commit(smem_u32(&sb.s_full[t]));
+                    }
+                    umma_commit(smem_u32(&sb.kv_empty[0]));
+                    ring = 1;
+                }
+            }
+            for (int j = 0; ok && j < n_max; ++j) {
+                const int v_slot = ring++;
+                const int vs = v_slot % STAGES;
+                const bool has_next = (j + 1 < n_max);
+                const int k_slot = has_next ? ring++ : 0;
+                const int ks = k_slot % STAGES;
+                const bool active = (j < n_kv[t]);
+                const bool next_s = (j + 1 < n_kv[t]);
+                bool k_ready = false;
+                if (active) {
+                    if constexpr (Cfg::SEP_P) {
+                        // S_t(j+1) as soon as the softmax has S_t(j) in registers.
+                        if (next_s) {
+                            ok = mbar_wait(smem_u32(&sb.s_free[t]), j & 1, wctx, kStatusTimeoutMma) &&
+                                 mbar_wait(smem_u32(&sb.kv_full[ks]), (k_slot / STAGES) & 1, wctx,
+                                           kStatusTimeoutMma);
+                            if (!ok) {
+                                break;
+                            }
+                            k_ready = true;
+                            tc_fence_after();
+                            issue_s_mma<Cfg>(s_addr, qd, kd0 + stage_off(ks));
+                            umma_commit(smem_u32(&sb.s_full[t]));
+                        }
+                    }
+                    ok = mbar_wait(smem_u32(&sb.p_full[t]), j & 1, wctx, kStatusTimeoutMma);
+                    if (j < 64) {
+                        FA_TRACE_AT(1024 + (t * 64 + j) * 4 + 0);
+                    }
+                    ok = ok && mbar_wait(smem_u32(&sb.kv_full[vs]), (v_slot / STAGES) & 1, wctx,
+                                         kStatusTimeoutMma);
+                    if (!ok) {
+                        break;
+                    }
+                    tc_fence_after();
+                    issue_pv_mma_f32<Cfg>(o_addr, p_addr, vd0 + stage_off(vs), j == 0);
+                    umma_commit(smem_u32(&sb.o_done[t]));
+                    if (j < 64) {
+                        FA_TRACE_AT(1024 + (t * 64 + j) * 4 + 1);
+                    }
+                    if constexpr (!Cfg::SEP_P) {
+                        // S_t(j+1) reuses the columns P_t(j) was read from by the MMAs above
+                        // (tcgen05.mma operations of one thread execute in issue order).
+                        if (next_s) {
+                            ok = mbar_wait(smem_u32(&sb.kv_full[ks]), (k_slot / STAGES) & 1, wctx,
+                                           kStatusTimeoutMma);
+                            if (!ok) {
+                                break;
+                            }
+                            k_ready = true;
+                            tc_fence_after();
+                            issue_s_mma<Cfg>(s_addr, qd, kd0 + stage_off(ks));
+                            umma_commit(smem_u32(&sb.s_full[t]));
+                            if (j < 64) {
+                                FA_TRACE_AT(1024 + (t * 64 + j) * 4 + 2);
+                            }
+                        }
+                    }
+                } else {
+                    ok = mbar_wait(smem_u32(&sb.kv_full[vs]), (v_slot / STAGES) & 1, wctx,
+                                   kStatusTimeoutMma);
+                }
+                if (ok && has_next && !k_ready) {
+                    ok = mbar_wait(smem_u32(&sb.kv_full[ks]), (k_slot / STAGES) & 1, wctx,
+                                   kStatusTimeoutMma);
+                }
+                if (!ok) {
+                    break;
+                }
+                umma_commit(smem_u32(&sb.kv_empty[vs]));
+                if (has_next) {
+                    umma_commit(smem_u32(&sb.kv_empty[ks]));
+                }
+            }
+            // Every MMA issued above must be complete before tensor memory is released.
+            umma_commit(smem_u32(&sb.mma_idle));
+            mbar_wait_drain(smem_u32(&sb.mma_idle), 0, wctx, kStatusTimeoutTeardown);
+        }
+        __syncwarp();
+    } else if (Cfg::kIssuers == 1 && warp == Cfg::kMmaWarp) {
         // ================================== MMA issuer ====================================
         if (lane == 0) {
             bool ok = true;

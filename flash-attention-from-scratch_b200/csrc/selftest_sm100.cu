@@ -190,7 +190,7 @@ __global__ void exp2_probe_kernel(const float* __restrict__ x, float* __restrict
 }
 
 // Watchdog probe: waits with the kernels' bounded wait (mbar_wait) on an mbarrier that no
-// thread ever arrives on. The wait must give up after kWaitTimeoutNs, record its code in the
+// thread ever arrives on. The wait must give up after 2^31 SM cycles, record its code in the
 // status word and let the kernel return; flags[0] = 1 if the wait reported failure, flags[1]
 // = 1 once the kernel reached its end.
 __global__ void watchdog_probe_kernel(int* flags) {

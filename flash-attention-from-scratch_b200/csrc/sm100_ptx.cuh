@@ -30,8 +30,9 @@ enum : unsigned {
     kStatusTimeoutTeardown = 1u << 4,  // teardown waited too long for in-flight async work
 };
 
-// A wait gives up after this many nanoseconds of %globaltimer. Every legitimate wait in the
-// kernel is a few microseconds; one second only trips on a real deadlock.
+// The teardown wait (mbar_wait_drain) gives up after this many nanoseconds of %globaltimer;
+// mbar_wait bounds its waits by 2^31 SM cycles (about as long). Every legitimate wait in the
+// kernel is a few microseconds; a second only trips on a real deadlock.
 constexpr unsigned long long kWaitTimeoutNs = 1000ull * 1000ull * 1000ull;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -88,32 +89,39 @@ struct WaitCtx {
 // time (after setting `code` in the global status, the CTA abort flag and the launch's abort
 // epoch), or when another thread of this CTA or another CTA of this launch has given up.
 // The result is per thread; callers that go on to warp-collective instructions vote on it.
+// The hot path polls shared memory only: the SM cycle counter bounds the wait (2^31 cycles,
+// about 1.1 s at the 1965 MHz boost clock and longer at lower clocks), and the global abort
+// epoch written by other CTAs is read only once a wait has lasted 2^20 cycles (~0.5 ms),
+// far beyond any wait of a healthy launch, so that a global load never delays a wake-up.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtx& w,
                                           unsigned code) {
     if (mbar_try_wait(bar, parity)) {
         return true;
     }
-    const unsigned long long t0 = globaltimer_ns();
+    const long long t0 = clock64();
     uint32_t spins = 0;
     while (true) {
         if (mbar_try_wait(bar, parity)) {
             return true;
         }
-        // The abort flags and the clock are checked every 32 polls only: a polling warp shares
+        // The abort flag and the clock are checked every 32 polls only: a polling warp shares
         // its SM sub-partition's issue slots with the warps doing the work.
         if ((++spins & 31u) == 0) {
             if (*w.cta_abort != 0) {
                 return false;
             }
-            if (*w.epoch_word == w.epoch) {
-                *w.cta_abort = 1;
-                return false;
-            }
-            if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
-                atomicOr(w.code_word, code);
-                *w.epoch_word = w.epoch;
-                *w.cta_abort = 1;
-                return false;
+            const long long waited = clock64() - t0;
+            if (waited > (1ll << 20)) {
+                if (*w.epoch_word == w.epoch) {
+                    *w.cta_abort = 1;
+                    return false;
+                }
+                if (waited > (1ll << 31)) {
+                    atomicOr(w.code_word, code);
+                    *w.epoch_word = w.epoch;
+                    *w.cta_abort = 1;
+                    return false;
+                }
             }
         }
     }
@@ -347,6 +355,23 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
     p = __ffma2_rn(p, f, make_float2(1.0f, 1.0f));
     // t's bits are 0x4B400000 + j; shifted left by 23 only j survives (mod 2^9), which adds j to
     // the exponent of p in [2^-1/2, 2^1/2].
+    return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                       __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+
+// Cheaper variant of exp2_poly2: degree-3 polynomial (fit_exp2_poly.py 3: max relative error
+// 1.0e-4 in float32, below the 2.4e-4 worst relative rounding of the fp16 value it feeds).
+__device__ __forceinline__ float2 exp2_poly2_deg3(float2 x) {
+    constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+    x.x = fmaxf(x.x, -126.0f);
+    x.y = fmaxf(x.y, -126.0f);
+    const float2 t = __fadd2_rn(x, make_float2(kRound, kRound));
+    const float2 r = __fadd2_rn(t, make_float2(-kRound, -kRound));
+    const float2 f = __ffma2_rn(r, make_float2(-1.0f, -1.0f), x);
+    float2 p = __ffma2_rn(make_float2(0.05500892922282219f, 0.05500892922282219f), f,
+                          make_float2(0.24221095442771912f, 0.24221095442771912f));
+    p = __ffma2_rn(p, f, make_float2(0.6932829022407532f, 0.6932829022407532f));
+    p = __ffma2_rn(p, f, make_float2(1.0f, 1.0f));
     return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
                        __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
 }
