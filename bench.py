@@ -1,6 +1,7 @@
 """Benchmark of the B200 FlashAttention-2 forward (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg1] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg1]
+                    [--impl ours|reference|reference-kernel]
     torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU)
 
 Metric: attention forward TFLOPS = 4 B H N^2 d / t, halved for causal (the reference's count,
@@ -19,6 +20,8 @@ fa/reference.py) on a bounded sample of heads of the same workload.
 
 --impl reference times the reference's own CPU path (its attention_reference, as the oracle
 port) on the host cores with every thread; under torchrun only rank 0 runs it.
+--impl reference-kernel (a context line) times the reference's own CUDA kernel compiled for
+sm_100a (baseline/build_ref_kernel.py) on the same workload and GPU.
 """
 
 from __future__ import annotations
@@ -260,6 +263,89 @@ def run_reference_arm(args, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_reference_kernel_arm(args, rank: int, world: int) -> None:
+    """--impl reference-kernel: a context line, not the driver's reference arm. Times the
+    reference's own CUDA kernel (mma.sync / ldmatrix / cp.async, written for sm_80+), compiled
+    unmodified for sm_100a by baseline/build_ref_kernel.py, on the same workload, GPU and clock
+    sampling as --impl ours. Rank 0 only."""
+    if rank != 0:
+        return
+    lib_path = REPO / "baseline" / "_ref" / "libfa_ref_kernel.so"
+    if not lib_path.exists():
+        print(json.dumps({"impl": "reference-kernel",
+                          "unavailable": "baseline/_ref/libfa_ref_kernel.so not built (needs the reference sources)"}))
+        return
+    import ctypes
+
+    import torch
+
+    from fa import _C
+    from fa.synthetic import attention_flops, make_qkv
+
+    lib = ctypes.CDLL(str(lib_path))
+    lib.fa_ref_kernel_fwd.restype = ctypes.c_int
+    lib.fa_ref_kernel_fwd.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 4 + [
+        ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int]
+    c = workload(args.workload)
+    variant = args.variant or c["variant"]
+    variant_id = {"baseline": 0, "opt": 1, "fp16acc": 2}[variant]
+    b, h, n, d, causal = c["b"], c["h"], c["n"], c["d"], c["causal"]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    q, k, v = make_qkv(b, h, n, d, c["seed"], scale=c["scale"], outliers=c.get("outliers", False))
+    qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+    od = torch.empty_like(qd)
+    stream = torch.cuda.current_stream(dev)
+    err = ctypes.create_string_buffer(512)
+    scale = 1.0 / math.sqrt(d)
+
+    def step():
+        rc = lib.fa_ref_kernel_fwd(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), od.data_ptr(), b, h, n, d,
+                                   scale, int(causal), variant_id, ctypes.c_void_p(stream.cuda_stream), err, 512)
+        if rc != 0:
+            raise SystemExit(f"reference kernel: {err.value.decode()}")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(0)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler.start()
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+    stop.record(stream)
+    stop.synchronize()
+    clocks = sampler.stop()
+    ms = start.elapsed_time(stop) / args.steps
+    # Same inputs through this repository's kernel, for the difference of the two outputs.
+    ours = _C.forward(qd, kd, vd, causal, None, variant)
+    diff = (ours.float() - od.float()).abs()
+    peaks, peak_kind = load_peaks()
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    flops = attention_flops(b, h, n, d, causal)
+    value = flops / (ms * 1e-3) / 1e12
+    print(json.dumps({
+        "impl": "reference-kernel",
+        "metric": "attn fwd TFLOPS (fp16, d=64/128, causal+non) at 1/2/4/8 B200; % of TC peak",
+        "value": value,
+        "unit": "TFLOPS",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "dtype": "f16",
+        "data": "synthetic (seeded N(0,1) fp16 inputs from a CPU generator)",
+        "config": {"workload": c["name"], "B": b, "H": h, "N": n, "d": d, "causal": causal, "variant": variant},
+        "pct_tc_peak": value / peak,
+        "peak_source": peak_kind,
+        "clocks": clocks,
+        "max_abs_diff_vs_ours": float(diff.max()),
+        "kernel": "reference csrc/kernels/flash_fwd.cu (mma.sync m16n8k16) built for sm_100a with the reference's nvcc flags",
+    }), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -267,7 +353,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--workload", default="cfg1")
     ap.add_argument("--variant", default=None, help="override the workload's kernel variant")
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-kernel"])
     ap.add_argument("--cpu-budget-s", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -280,6 +366,9 @@ def main() -> None:
 
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
+        return
+    if args.impl == "reference-kernel":
+        run_reference_kernel_arm(args, rank, world)
         return
 
     import torch
