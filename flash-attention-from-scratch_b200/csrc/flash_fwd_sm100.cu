@@ -78,6 +78,9 @@
 #ifndef FA_MMA_ISSUERS_D128
 #define FA_MMA_ISSUERS_D128 1
 #endif
+#ifndef FA_MMA_ISSUERS_ACC16
+#define FA_MMA_ISSUERS_ACC16 1
+#endif
 #ifndef FA_SPLIT_COLS
 #define FA_SPLIT_COLS 1
 #endif
@@ -100,8 +103,12 @@ struct FwdCfg {
     // Lazy rescale (reference LAZY, flash_fwd.cu:365-376): keep a stale row max until the
     // tile max exceeds it by more than 2^8. Threshold 0 = exact running max.
     static constexpr float kRescaleThreshold = (VARIANT_ == kVariantOpt) ? 8.0f : 0.0f;
-    static constexpr int NQ = ACC16 ? 1 : 2;
+    // Query tiles per CTA. fp16acc at d = 128 needs S + O + 2 T = 512 columns for one tile.
+    static constexpr int NQ = (ACC16 && D == 128) ? 1 : 2;
     static constexpr bool SEP_P = !ACC16 && D == 64;
+    // fp16acc with two tiles (d = 64): T_1 (keys 64..127) lives in S_t's upper 64 columns,
+    // free once the softmax has read S_t and written P_t into the lower 64.
+    static constexpr bool T_HI_IN_S = ACC16 && NQ == 2;
     static constexpr int kEmuPer8 = ACC16 ? 0 : (D == 128 ? FA_EMU_PER8_D128 : FA_EMU_PER8_D64);
     static constexpr int kTileBytes = kBM * D * 2;  // one Q, K, V or O tile (BM == BN)
     static constexpr int kBoxes = D / 64;           // TMA boxes per tile
@@ -115,7 +122,11 @@ struct FwdCfg {
     static constexpr int kTmemS = 0;
     static constexpr int kTmemO = NQ * kBN;
     static constexpr int kTmemExtra = kTmemO + NQ * D;  // P_t (SEP_P) or T_h (ACC16)
-    static constexpr int kTmemUsed = kTmemExtra + (ACC16 ? 2 * D : (SEP_P ? NQ * 64 : 0));
+    static constexpr int kTmemUsed =
+        kTmemExtra + (T_HI_IN_S ? NQ * D : (ACC16 ? 2 * D : (SEP_P ? NQ * 64 : 0)));
+    // fp16acc partials of tile t: T_0 over keys [0, 64), T_1 over keys [64, 128).
+    static constexpr int tmem_t0(int t) { return kTmemExtra + (T_HI_IN_S ? D * t : 0); }
+    static constexpr int tmem_t1(int t) { return T_HI_IN_S ? (kTmemS + kBN * t + 64) : (kTmemExtra + D); }
     static constexpr int kTmemCols = 512;
     static_assert(kTmemUsed <= kTmemCols, "tensor memory budget");
     // Warps: NQ x SPLIT softmax warpgroups + one producer/MMA warpgroup. With SPLIT = 2 the
@@ -126,13 +137,17 @@ struct FwdCfg {
     static constexpr int kProducerWarp = kSoftmaxWarps;
     static constexpr int kMmaWarp = kSoftmaxWarps + 1;
     static constexpr int kIssuers =  // MMA issuer warps kMmaWarp + i
-        (NQ == 2 && (D == 64 ? FA_MMA_ISSUERS_D64 : FA_MMA_ISSUERS_D128) == 2) ? 2 : 1;
+        (NQ == 2 && (ACC16 ? FA_MMA_ISSUERS_ACC16 : (D == 64 ? FA_MMA_ISSUERS_D64 : FA_MMA_ISSUERS_D128)) == 2)
+            ? 2
+            : 1;
     static constexpr int kThreads = 32 * (kSoftmaxWarps + 4);
     // Register split: every warp is launched with kRegsLaunch (65536 / threads, a multiple of
     // 8); with FA_REGS_SOFTMAX != 0 the softmax warpgroups go to that many and the
     // producer/MMA warpgroup gives up the difference.
     static constexpr int kRegsLaunch = ((65536 / kThreads) / 8 * 8) > 255 ? 248 : (65536 / kThreads) / 8 * 8;
-    static constexpr int kRegsSoftmax = FA_REGS_SOFTMAX;
+    // fp16acc with two tiles: its softmax (exponentials, then the fold of two fp16 partials)
+    // spills at the launch share of 168, so it takes 200 from the producer/MMA warpgroup.
+    static constexpr int kRegsSoftmax = T_HI_IN_S ? 200 : FA_REGS_SOFTMAX;
     static constexpr int kRegsOther =
         kRegsSoftmax == 0
             ? kRegsLaunch
@@ -175,6 +190,7 @@ struct SharedBarriers {
 // [1024, +2*4*64): MMA t: {P ready, PV issued, S(j+1) issued, V ready}
 // [2048, +256): producer ring slot: load issued
 // [2304, +2*4*64): softmax t, key tile j: arrival on P-ready of each of the tile's four warps
+// [2816, +2*4*64): fp16acc softmax t, key tile j: fold of the fp16 partials done (slot 0)
 __device__ unsigned long long g_fa_trace[4096];
 __device__ __forceinline__ bool trace_cta() {
     return blockIdx.x == gridDim.x / 2 && blockIdx.y == 0;
@@ -228,14 +244,15 @@ __device__ __forceinline__ void issue_pv_mma_f32(uint32_t tmem_o, uint32_t tmem_
 
 // fp16acc: T_h = P[:, 64h:64h+64] V[64h:64h+64, :] accumulated in fp16, fresh per tile.
 template <class Cfg>
-__device__ __forceinline__ void issue_pv_mma_f16(uint32_t tmem_t, uint32_t tmem_p, uint64_t vd) {
+__device__ __forceinline__ void issue_pv_mma_f16(uint32_t tmem_t0, uint32_t tmem_t1, uint32_t tmem_p,
+                                                 uint64_t vd) {
     constexpr uint32_t idesc = make_idesc_f16(kBM, Cfg::D, /*d_f32=*/false, /*b_mn_major=*/true);
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
 #pragma unroll
         for (int k4 = 0; k4 < 4; ++k4) {
             const int kk = h * 4 + k4;
-            umma_ts(tmem_t + h * Cfg::D, tmem_p + kk * 8, vd + static_cast<uint64_t>(kk * (2048 >> 4)),
+            umma_ts(h == 0 ? tmem_t0 : tmem_t1, tmem_p + kk * 8, vd + static_cast<uint64_t>(kk * (2048 >> 4)),
                     idesc, k4 == 0 ? 0u : 1u);
         }
     }
@@ -382,7 +399,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         const uint32_t t_o = tmem + lane_off + Cfg::kTmemO + t * D + half * OC;
         const uint32_t t_p = (Cfg::SEP_P ? (tmem + lane_off + Cfg::kTmemExtra + t * 64)
                                          : (tmem + lane_off + Cfg::kTmemS + t * kBN)) + col0 / 2;
-        const uint32_t t_t = tmem + lane_off + Cfg::kTmemExtra;
+        const uint32_t t_t0 = tmem + lane_off + Cfg::tmem_t0(t);
+        const uint32_t t_t1 = tmem + lane_off + Cfg::tmem_t1(t);
         const uint32_t bar_s = smem_u32(&sb.s_full[t]);
         const uint32_t bar_sf = smem_u32(&sb.s_free[t]);
         const uint32_t bar_p = smem_u32(&sb.p_full[t]);
@@ -562,6 +580,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 if (lane == 0) {
                     mbar_arrive(bar_p);
                 }
+                if (row == 0 && j < 64) {
+                    FA_TRACE_AT((t * 64 + j) * 4 + 2);
+                }
                 // Fold this tile's two fp16 partials into the fp32 accumulator:
                 // O = alpha * O + T_0 + T_1.
                 ok = __all_sync(0xffffffffu, mbar_wait(bar_o, j & 1, wctx, kStatusTimeoutSoftmax));
@@ -569,13 +590,14 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     continue;
                 }
                 tc_fence_after();
-#pragma unroll
+                // One 32-column chunk at a time (three 32-register loads in flight).
+#pragma unroll 1
                 for (int c = 0; c < D / 32; ++c) {
                     uint32_t a[32];
                     uint32_t b[32];
                     uint32_t o[32];
-                    tmem_ld32(t_t + c * 32, a);
-                    tmem_ld32(t_t + D + c * 32, b);
+                    tmem_ld32(t_t0 + c * 32, a);
+                    tmem_ld32(t_t1 + c * 32, b);
                     if (j > 0) {
                         tmem_ld32(t_o + c * 32, o);
                     }
@@ -588,6 +610,17 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     tmem_st32(t_o + c * 32, o);
                 }
                 tmem_wait_st();
+                if constexpr (Cfg::T_HI_IN_S) {
+                    // T_1 has been read out of S_t's columns: S_t(j+1) may overwrite them.
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(bar_sf);
+                    }
+                }
+                if (row == 0 && j < 64) {
+                    FA_TRACE_AT(2816 + (t * 64 + j) * 4);
+                }
             }
         }
 
@@ -774,6 +807,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                             tc_fence_after();
                             issue_s_mma<Cfg>(s_addr, qd, kd0 + stage_off(ks));
                             umma_commit(smem_u32(&sb.s_full[t]));
+                            if (j < 64) {
+                                FA_TRACE_AT(1024 + (t * 64 + j) * 4 + 2);
+                            }
                         }
                     }
                     ok = mbar_wait(smem_u32(&sb.p_full[t]), j & 1, wctx, kStatusTimeoutMma);
@@ -786,17 +822,26 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    issue_pv_mma_f32<Cfg>(o_addr, p_addr, vd0 + stage_off(vs), j == 0);
+                    if constexpr (Cfg::ACC16) {
+                        issue_pv_mma_f16<Cfg>(tmem + Cfg::tmem_t0(t), tmem + Cfg::tmem_t1(t), p_addr,
+                                              vd0 + stage_off(vs));
+                    } else {
+                        issue_pv_mma_f32<Cfg>(o_addr, p_addr, vd0 + stage_off(vs), j == 0);
+                    }
                     umma_commit(smem_u32(&sb.o_done[t]));
                     if (j < 64) {
                         FA_TRACE_AT(1024 + (t * 64 + j) * 4 + 1);
                     }
                     if constexpr (!Cfg::SEP_P) {
                         // S_t(j+1) reuses the columns P_t(j) was read from by the MMAs above
-                        // (tcgen05.mma operations of one thread execute in issue order).
+                        // (tcgen05.mma operations of one thread execute in issue order); with
+                        // fp16acc also those of T_1, once the softmax has folded it into O.
                         if (next_s) {
-                            ok = mbar_wait(smem_u32(&sb.kv_full[ks]), (k_slot / STAGES) & 1, wctx,
-                                           kStatusTimeoutMma);
+                            if constexpr (Cfg::T_HI_IN_S) {
+                                ok = mbar_wait(smem_u32(&sb.s_free[t]), j & 1, wctx, kStatusTimeoutMma);
+                            }
+                            ok = ok && mbar_wait(smem_u32(&sb.kv_full[ks]), (k_slot / STAGES) & 1, wctx,
+                                                 kStatusTimeoutMma);
                             if (!ok) {
                                 break;
                             }
@@ -914,7 +959,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     tc_fence_after();
                     const uint64_t vd = vd0 + stage_off(vs);
                     if constexpr (Cfg::ACC16) {
-                        issue_pv_mma_f16<Cfg>(tmem + Cfg::kTmemExtra, s_addr, vd);
+                        issue_pv_mma_f16<Cfg>(tmem + Cfg::tmem_t0(t), tmem + Cfg::tmem_t1(t), s_addr, vd);
                     } else if constexpr (Cfg::SEP_P) {
                         issue_pv_mma_f32<Cfg>(tmem + Cfg::kTmemO + t * Cfg::D,
                                               tmem + Cfg::kTmemExtra + t * 64, vd, j == 0);
@@ -926,8 +971,15 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                         FA_TRACE_AT(1024 + (t * 64 + j) * 4 + 1);
                     }
                     if constexpr (!Cfg::SEP_P) {
-                        // S_t(j+1) reuses the columns P_t(j) was read from by the MMAs above.
+                        // S_t(j+1) reuses the columns P_t(j) was read from by the MMAs above;
+                        // with fp16acc also those of T_1, once the softmax has folded it into O.
                         if (next_s) {
+                            if constexpr (Cfg::T_HI_IN_S) {
+                                ok = mbar_wait(smem_u32(&sb.s_free[t]), j & 1, wctx, kStatusTimeoutMma);
+                                if (!ok) {
+                                    break;
+                                }
+                            }
                             if (!k_ready) {
                                 ok = mbar_wait(smem_u32(&sb.kv_full[ks]), (k_slot / STAGES) & 1,
                                                wctx, kStatusTimeoutMma);
