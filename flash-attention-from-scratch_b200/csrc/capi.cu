@@ -8,6 +8,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdint>
@@ -97,10 +98,26 @@ int validate(const FaFwdParams* p) {
     return FA_OK;
 }
 
-int launch_one(const FaFwdParams* p, cudaStream_t stream) {
+constexpr int kMaxSplits = 64;
+
+int launch_one(const FaFwdParams* p, cudaStream_t stream, int num_splits = 1,
+               void* workspace = nullptr, uint64_t workspace_bytes = 0) {
     const int rc = validate(p);
     if (rc != FA_OK) {
         return rc;
+    }
+    if (num_splits < 1 || num_splits > kMaxSplits) {
+        return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd_splitkv: num_splits must be in 1 .. 64, got " +
+                                                 std::to_string(num_splits));
+    }
+    if (num_splits > 1) {
+        const uint64_t need = fa_sm100::splitkv_workspace_bytes(p->batch * p->heads, p->seqlen,
+                                                                p->head_dim, num_splits);
+        if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)) {
+            return fail(FA_ERR_INVALID_ARGUMENT,
+                        "flash_fwd_splitkv: workspace must be 16-byte aligned and hold at least " +
+                            std::to_string(need) + " bytes");
+        }
     }
     int device = 0;
     cudaError_t err = cudaGetDevice(&device);
@@ -129,12 +146,25 @@ int launch_one(const FaFwdParams* p, cudaStream_t stream) {
     args.scale_log2 = static_cast<float>(static_cast<double>(p->softmax_scale) * M_LOG2E);
     args.epoch = next_epoch();
     args.status = status;
+    args.num_splits = num_splits;
+    args.rows_pad = (p->seqlen + 255) / 256 * 256;
+    if (num_splits > 1) {
+        const uint64_t recs = static_cast<uint64_t>(num_splits) * bh * args.rows_pad;
+        args.ws_o = static_cast<float*>(workspace);
+        args.ws_ml = args.ws_o + recs * p->head_dim;
+    }
     err = fa_sm100::launch_forward(prob, args, stream);
     if (err == cudaErrorInvalidValue) {
         return fail(FA_ERR_CUDA, "flash_fwd: cuTensorMapEncodeTiled failed");
     }
     if (err != cudaSuccess) {
         return cuda_fail(err, "kernel launch");
+    }
+    if (num_splits > 1) {
+        err = fa_sm100::launch_splitkv_combine(prob, args, stream);
+        if (err != cudaSuccess) {
+            return cuda_fail(err, "split-KV combine launch");
+        }
     }
     g_last_error.clear();
     return FA_OK;
@@ -205,6 +235,57 @@ int fa_device_status(int32_t device, int32_t clear, uint32_t* status_out) {
         *status_out = host.code;
     }
     return FA_OK;
+}
+
+int fa_splitkv_workspace_size(const FaFwdParams* params, int32_t num_splits, uint64_t* bytes_out) {
+    const int rc = validate(params);
+    if (rc != FA_OK) {
+        return rc;
+    }
+    if (num_splits < 1 || num_splits > kMaxSplits) {
+        return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd_splitkv: num_splits must be in 1 .. 64, got " +
+                                                 std::to_string(num_splits));
+    }
+    if (bytes_out != nullptr) {
+        *bytes_out = num_splits == 1 ? 0
+                                     : fa_sm100::splitkv_workspace_bytes(params->batch * params->heads,
+                                                                         params->seqlen, params->head_dim,
+                                                                         num_splits);
+    }
+    g_last_error.clear();
+    return FA_OK;
+}
+
+int fa_splitkv_choose(const FaFwdParams* params, int32_t num_sms, int32_t* num_splits_out) {
+    const int rc = validate(params);
+    if (rc != FA_OK) {
+        return rc;
+    }
+    if (num_sms <= 0) {
+        return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd_splitkv: num_sms must be positive");
+    }
+    const int rows_per_cta = fa_sm100::kernel_rows_per_cta(params->head_dim, params->variant);
+    const int64_t ctas = static_cast<int64_t>((params->seqlen + rows_per_cta - 1) / rows_per_cta) *
+                         params->batch * params->heads;
+    const int key_tiles = (params->seqlen + 127) / 128;
+    int splits = 1;
+    if (ctas < num_sms) {
+        splits = static_cast<int>(num_sms / ctas);
+        splits = std::min(splits, std::max(1, key_tiles / 2));
+        splits = std::min(splits, 16);
+        splits = std::max(splits, 1);
+    }
+    if (num_splits_out != nullptr) {
+        *num_splits_out = splits;
+    }
+    g_last_error.clear();
+    return FA_OK;
+}
+
+int fa_flash_fwd_splitkv(const FaFwdParams* params, int32_t num_splits, void* workspace,
+                         uint64_t workspace_bytes, fa_stream_t stream) {
+    return launch_one(params, reinterpret_cast<cudaStream_t>(stream), num_splits, workspace,
+                      workspace_bytes);
 }
 
 int fa_kernel_info(int32_t head_dim, int32_t variant, int32_t* smem_bytes, int32_t* threads) {

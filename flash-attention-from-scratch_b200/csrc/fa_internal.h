@@ -23,7 +23,21 @@ struct FwdArgs {
     unsigned epoch;       // launch epoch, never 0
     DeviceStatus* status; // per-device watchdog record
     int head_group;       // causal schedule: heads interleaved in one heavy-first sweep (>= 1)
+    // Split-KV (num_splits > 1): CTA (x, y, z) covers the z-th of num_splits contiguous
+    // ranges of its row block's key tiles and writes, per row, its unnormalised fp32 O and
+    // (m, l) to the workspace instead of O; a combine kernel merges the splits.
+    int num_splits;       // 1 = no split
+    int rows_pad;         // workspace rows per head: ceil(N / 256) * 256
+    float* ws_o;          // [num_splits][num_bh][rows_pad][D] fp32
+    float* ws_ml;         // [num_splits][num_bh][rows_pad][2] fp32: m (log2 units), l
 };
+
+// Split-KV workspace bytes for a problem (16-byte aligned sections).
+inline unsigned long long splitkv_workspace_bytes(int num_bh, int seqlen, int head_dim, int num_splits) {
+    const unsigned long long rows = static_cast<unsigned long long>((seqlen + 255) / 256) * 256;
+    const unsigned long long recs = rows * static_cast<unsigned long long>(num_bh) * num_splits;
+    return recs * head_dim * 4ull + recs * 2ull * 4ull;
+}
 
 // Variant ids as in the reference (csrc/flash_fwd.h:12-16).
 enum : int { kVariantBaseline = 0, kVariantOpt = 1, kVariantFp16Acc = 2 };
@@ -41,6 +55,9 @@ struct FwdProblem {
     int variant;
 };
 
+// Launches the split-KV combine: O[bh][row] = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s, fp16.
+cudaError_t launch_splitkv_combine(const FwdProblem& prob, const FwdArgs& args, cudaStream_t stream);
+
 // Encodes the TMA tensor maps the chosen kernel needs and launches it on `stream`.
 // Returns cudaSuccess, a CUDA launch error, or cudaErrorInvalidValue if a tensor map could not
 // be encoded.
@@ -49,5 +66,7 @@ cudaError_t launch_forward(const FwdProblem& prob, const FwdArgs& args, cudaStre
 // Shared-memory bytes and threads per CTA of a kernel instantiation (for reports / tests).
 int kernel_smem_bytes(int head_dim, bool causal, int variant);
 int kernel_threads(int head_dim, bool causal, int variant);
+// Query rows per CTA (128 * query tiles per CTA).
+int kernel_rows_per_cta(int head_dim, int variant);
 
 }  // namespace fa_sm100

@@ -329,6 +329,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     }
     const int q_row0 = m_block * NQ * kBM;
     const int n_tiles_all = (n + kBN - 1) / kBN;
+    // n_kv[t]: key tiles tile t processes in this CTA, starting at absolute key tile kv0.
     int n_kv[NQ];
     int n_max = 0;
 #pragma unroll
@@ -336,6 +337,18 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         const int q0 = q_row0 + t * kBM;
         n_kv[t] = (q0 >= n) ? 0 : (Cfg::CAUSAL ? (q0 / kBN + 1) : n_tiles_all);
         n_max = max(n_max, n_kv[t]);
+    }
+    int kv0 = 0;
+    const bool split = args.num_splits > 1;
+    if (split) {
+        // The block's key tiles [0, n_max) in num_splits contiguous ranges; range z here.
+        const int per = (n_max + args.num_splits - 1) / args.num_splits;
+        kv0 = static_cast<int>(blockIdx.z) * per;
+#pragma unroll
+        for (int t = 0; t < NQ; ++t) {
+            n_kv[t] = max(0, min(n_kv[t] - kv0, per));
+        }
+        n_max = max(0, min(n_max - kv0, per));
     }
 
     const WaitCtx wctx{&sb.abort, &args.status->code, &args.status->epoch_aborted, args.epoch};
@@ -446,10 +459,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 }
             }
 
-            const int kbase = j * kBN;
-            // Only the last tile can hold keys >= N, and for causal rows only the last tile
-            // (the diagonal one) holds keys after the row: every other tile is unmasked.
-            const bool masked = (kbase + kBN > n) || (Cfg::CAUSAL && j == nt - 1);
+            const int kbase = (kv0 + j) * kBN;
+            // Only the last key tile can hold keys >= N, and for causal rows only the diagonal
+            // tile (key tile q0 / 128) holds keys after the row: every other tile is unmasked.
+            const bool masked = (kbase + kBN > n) || (Cfg::CAUSAL && kbase == q0);
             float tile_max;
             float mul;
             if (masked) {
@@ -640,7 +653,39 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             pair_sync(pair_id);
             row_sum += rs.red_sum[t][half ^ 1][row];
         }
-        if (ok && nt > 0) {
+        if (split) {
+            // Split-KV: the row's unnormalised O over this CTA's key range and its (m, l) go to
+            // the workspace; a range with no keys for this tile records l = 0, which the
+            // combine skips. Every record of a row that exists (q0 < N) is written, so the
+            // workspace needs no initialisation.
+            if (q0 < n && (ok || nt == 0)) {
+                const size_t rec =
+                    (static_cast<size_t>(blockIdx.z) * args.num_bh + bh) * args.rows_pad + grow;
+                float4* dst = reinterpret_cast<float4*>(args.ws_o + rec * D + half * OC);
+                if (nt > 0) {
+#pragma unroll
+                    for (int c = 0; c < OC / 32; ++c) {
+                        uint32_t o[32];
+                        tmem_ld32(t_o + c * 32, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            dst[c * 8 + i] = make_float4(u2f(o[4 * i]), u2f(o[4 * i + 1]),
+                                                         u2f(o[4 * i + 2]), u2f(o[4 * i + 3]));
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < OC / 4; ++i) {
+                        dst[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    }
+                }
+                if (half == 0) {
+                    reinterpret_cast<float2*>(args.ws_ml)[rec] =
+                        make_float2(nt > 0 ? row_max : -INFINITY, nt > 0 ? row_sum : 0.0f);
+                }
+            }
+        } else if (ok && nt > 0) {
             const float inv_sum = (row_sum > 0.0f) ? (1.0f / row_sum) : 0.0f;
             // Stage O (fp16) in this tile's Q buffer, in the swizzled layout of the TMA box.
             // Every MMA that read Q_t has completed (its S was consumed above).
@@ -723,7 +768,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 #pragma unroll
                     for (int b = 0; b < Cfg::kBoxes; ++b) {
                         tma_load_3d(smem_base + Cfg::kSmemKV + stage * Cfg::kTileBytes + b * kBoxBytes,
-                                    map, bar, b * 64, j * kBN, bh);
+                                    map, bar, b * 64, (kv0 + j) * kBN, bh);
                     }
                     loaded[stage] = true;
                     last_parity[stage] = phase;
@@ -1020,6 +1065,67 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     }
 }
 
+// Split-KV combine (reference: none; Flash-Decoding's merge of per-range softmax partials).
+// One warp per (head, row), lanes over the head dim, splits merged in index order (so the
+// result is deterministic): M = max m_s over splits with l_s > 0, then
+// O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s, rounded to fp16.
+template <int D>
+__global__ void __launch_bounds__(256) splitkv_combine_kernel(const float* __restrict__ ws_o,
+                                                              const float2* __restrict__ ws_ml,
+                                                              __half* __restrict__ o, int num_bh,
+                                                              int n, int rows_pad, int num_splits) {
+    constexpr int PER = D / 32;  // columns per lane
+    const long long item = static_cast<long long>(blockIdx.x) * 8 + threadIdx.x / 32;
+    const int lane = static_cast<int>(threadIdx.x) % 32;
+    if (item >= static_cast<long long>(num_bh) * n) {
+        return;
+    }
+    const int bh = static_cast<int>(item / n);
+    const int row = static_cast<int>(item - static_cast<long long>(bh) * n);
+    float m_max = -INFINITY;
+    for (int sp = 0; sp < num_splits; ++sp) {
+        const float2 ml = ws_ml[(static_cast<size_t>(sp) * num_bh + bh) * rows_pad + row];
+        if (ml.y > 0.0f) {
+            m_max = fmaxf(m_max, ml.x);
+        }
+    }
+    float acc[PER];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+        acc[i] = 0.0f;
+    }
+    float l = 0.0f;
+    for (int sp = 0; sp < num_splits; ++sp) {
+        const size_t rec = (static_cast<size_t>(sp) * num_bh + bh) * rows_pad + row;
+        const float2 ml = ws_ml[rec];
+        if (!(ml.y > 0.0f)) {
+            continue;
+        }
+        const float w = exp2f(ml.x - m_max);
+        l = fmaf(ml.y, w, l);
+        const float* src = ws_o + rec * D + lane * PER;
+        if constexpr (PER == 4) {
+            const float4 v = *reinterpret_cast<const float4*>(src);
+            acc[0] = fmaf(v.x, w, acc[0]);
+            acc[1] = fmaf(v.y, w, acc[1]);
+            acc[2] = fmaf(v.z, w, acc[2]);
+            acc[3] = fmaf(v.w, w, acc[3]);
+        } else {
+            const float2 v = *reinterpret_cast<const float2*>(src);
+            acc[0] = fmaf(v.x, w, acc[0]);
+            acc[1] = fmaf(v.y, w, acc[1]);
+        }
+    }
+    const float inv = (l > 0.0f) ? (1.0f / l) : 0.0f;
+    __half* dst = o + (static_cast<size_t>(bh) * n + row) * D + lane * PER;
+    if constexpr (PER == 4) {
+        *reinterpret_cast<uint2*>(dst) =
+            make_uint2(pack_half2(acc[0] * inv, acc[1] * inv), pack_half2(acc[2] * inv, acc[3] * inv));
+    } else {
+        *reinterpret_cast<uint32_t*>(dst) = pack_half2(acc[0] * inv, acc[1] * inv);
+    }
+}
+
 // ------------------------------------------------------------------------------------------
 // Host-side dispatch
 // ------------------------------------------------------------------------------------------
@@ -1041,7 +1147,8 @@ cudaError_t launch_cfg(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const C
     launch_args.head_group =
         static_cast<int>(std::min<double>(args.num_bh, std::max(1.0, (48.0 * 1048576.0) / kv_bytes)));
     const dim3 grid(static_cast<unsigned>((args.seqlen + rows_per_cta - 1) / rows_per_cta),
-                    static_cast<unsigned>(args.num_bh));
+                    static_cast<unsigned>(args.num_bh),
+                    static_cast<unsigned>(args.num_splits > 1 ? args.num_splits : 1));
     kernel<<<grid, Cfg::kThreads, Cfg::kSmemAlloc, stream>>>(tm_q, tm_k, tm_v, tm_o, launch_args);
     return cudaGetLastError();
 }
@@ -1110,12 +1217,34 @@ int threads_for(int variant) {
     }
 }
 
+cudaError_t launch_splitkv_combine(const FwdProblem& prob, const FwdArgs& args, cudaStream_t stream) {
+    const long long items = static_cast<long long>(prob.num_bh) * prob.seqlen;
+    const dim3 grid(static_cast<unsigned>((items + 7) / 8));
+    auto* out = static_cast<__half*>(prob.o);
+    const auto* ml = reinterpret_cast<const float2*>(args.ws_ml);
+    if (prob.head_dim == 64) {
+        splitkv_combine_kernel<64><<<grid, 256, 0, stream>>>(args.ws_o, ml, out, prob.num_bh,
+                                                             prob.seqlen, args.rows_pad, args.num_splits);
+    } else {
+        splitkv_combine_kernel<128><<<grid, 256, 0, stream>>>(args.ws_o, ml, out, prob.num_bh,
+                                                              prob.seqlen, args.rows_pad, args.num_splits);
+    }
+    return cudaGetLastError();
+}
+
 int kernel_smem_bytes(int head_dim, bool /*causal*/, int variant) {
     return head_dim == 64 ? smem_for<64>(variant) : smem_for<128>(variant);
 }
 
 int kernel_threads(int head_dim, bool /*causal*/, int variant) {
     return head_dim == 64 ? threads_for<64>(variant) : threads_for<128>(variant);
+}
+
+int kernel_rows_per_cta(int head_dim, int variant) {
+    const bool acc16 = variant == kVariantFp16Acc;
+    return kBM * (head_dim == 64 ? FwdCfg<64, false, kVariantOpt>::NQ
+                                 : (acc16 ? FwdCfg<128, false, kVariantFp16Acc>::NQ
+                                          : FwdCfg<128, false, kVariantOpt>::NQ));
 }
 
 #ifdef FA_TRACE

@@ -76,6 +76,15 @@ def _load() -> ctypes.CDLL:
         ctypes.POINTER(ctypes.c_int32),
     ]
     lib.fa_kernel_info.restype = ctypes.c_int
+    lib.fa_splitkv_workspace_size.argtypes = [
+        ctypes.POINTER(FaFwdParams), ctypes.c_int32, ctypes.POINTER(ctypes.c_uint64)]
+    lib.fa_splitkv_workspace_size.restype = ctypes.c_int
+    lib.fa_splitkv_choose.argtypes = [
+        ctypes.POINTER(FaFwdParams), ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)]
+    lib.fa_splitkv_choose.restype = ctypes.c_int
+    lib.fa_flash_fwd_splitkv.argtypes = [
+        ctypes.POINTER(FaFwdParams), ctypes.c_int32, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]
+    lib.fa_flash_fwd_splitkv.restype = ctypes.c_int
     return lib
 
 
@@ -123,6 +132,25 @@ def make_params(q, k, v, o, causal: bool, softmax_scale: float, variant: int) ->
     return p
 
 
+_SM_COUNT: dict[int, int] = {}
+
+
+def _sm_count(device: torch.device) -> int:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _SM_COUNT:
+        _SM_COUNT[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return _SM_COUNT[idx]
+
+
+def choose_splits(params: FaFwdParams, device: torch.device) -> int:
+    """Split count the library picks for `params` on `device` (1 = no split)."""
+    out = ctypes.c_int32(1)
+    rc = lib.fa_splitkv_choose(ctypes.byref(params), _sm_count(device), ctypes.byref(out))
+    if rc != FA_OK:
+        _raise(rc)
+    return int(out.value)
+
+
 def forward(
     q: torch.Tensor,
     k: torch.Tensor,
@@ -131,7 +159,23 @@ def forward(
     softmax_scale: float | None = None,
     variant: str = "opt",
 ) -> torch.Tensor:
-    """O = softmax(Q K^T * scale) V (reference csrc/bindings.cpp:28-64)."""
+    """O = softmax(Q K^T * scale) V (reference csrc/bindings.cpp:28-64). The library picks the
+    split-KV count (1 whenever the row blocks already fill the GPU)."""
+    return forward_splitkv(q, k, v, causal, softmax_scale, variant, None)
+
+
+def forward_splitkv(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    causal: bool = False,
+    softmax_scale: float | None = None,
+    variant: str = "opt",
+    num_splits: int | None = None,
+) -> torch.Tensor:
+    """forward() with an explicit split-KV count (not in the reference): each row block's key
+    range is cut into ``num_splits`` ranges (None = the library's choice). The workspace is a
+    torch allocation on the current stream, like O itself."""
     check_inputs(q, k, v)
     with torch.cuda.device(q.device):
         o = torch.empty_like(q)
@@ -141,7 +185,16 @@ def forward(
         if q.shape[2] > 0:
             params = make_params(q, k, v, o, causal, scale, vid)
             stream = torch.cuda.current_stream(q.device).cuda_stream
-            rc = lib.fa_flash_fwd(ctypes.byref(params), ctypes.c_void_p(stream))
+            splits = choose_splits(params, q.device) if num_splits is None else int(num_splits)
+            if splits == 1:
+                rc = lib.fa_flash_fwd(ctypes.byref(params), ctypes.c_void_p(stream))
+            else:
+                nbytes = ctypes.c_uint64(0)
+                rc = lib.fa_splitkv_workspace_size(ctypes.byref(params), splits, ctypes.byref(nbytes))
+                if rc == FA_OK:
+                    ws = torch.empty(int(nbytes.value), dtype=torch.uint8, device=q.device)
+                    rc = lib.fa_flash_fwd_splitkv(ctypes.byref(params), splits, ctypes.c_void_p(ws.data_ptr()),
+                                                  nbytes.value, ctypes.c_void_p(stream))
             if rc != FA_OK:
                 _raise(rc)
     return o

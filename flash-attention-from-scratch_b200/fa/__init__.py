@@ -5,8 +5,9 @@
     o = fa.forward(q, k, v, fp16_accum=True)   # P.V accumulated in fp16 per 64 keys
 
 Same public surface as the reference package (fa/__init__.py:14-38): ``forward``,
-``forward_variant`` and ``attention_reference``. The kernel is tcgen05 / TMEM / TMA code for
-sm_100a in libfa_b200.so; there is no CPU or fallback path.
+``forward_variant`` and ``attention_reference``; plus ``forward_splitkv`` and the multi-GPU
+``forward_sharded`` / ``plan_shards``. The kernel is tcgen05 / TMEM / TMA code for sm_100a in
+libfa_b200.so; there is no CPU or fallback path.
 """
 
 import torch
@@ -41,4 +42,21 @@ def forward_variant(
     return _C.forward(q, k, v, causal, None, variant)
 
 
-__all__ = ["forward", "forward_variant", "attention_reference", "forward_sharded", "plan_shards"]
+def forward_splitkv(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    causal: bool = False,
+    softmax_scale: float | None = None,
+    num_splits: int | None = None,
+    variant: str = "opt",
+) -> torch.Tensor:
+    """forward() with each row block's key range cut into ``num_splits`` ranges that run as
+    separate CTAs and are merged by a second kernel (not in the reference; it lists split-KV
+    as not done). None picks the count the library would use inside forward(): 1 unless the
+    row blocks leave SMs idle (few heads x long N)."""
+    return _C.forward_splitkv(q, k, v, causal, softmax_scale, variant, num_splits)
+
+
+__all__ = ["forward", "forward_variant", "forward_splitkv", "attention_reference", "forward_sharded",
+           "plan_shards"]

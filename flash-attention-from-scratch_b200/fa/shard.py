@@ -70,7 +70,9 @@ def forward_sharded(
     """Runs every shard on its own GPU with one launcher call; returns the per-shard outputs.
 
     Each q_parts[i], k_parts[i], v_parts[i] is a [b_i, h_i, N, d] fp16 CUDA tensor on one device
-    (see split_heads). The call is asynchronous on each device's current stream.
+    (see split_heads). The call is asynchronous on each device's current stream. Shards run
+    unsplit (one range of keys per row block, as fa.forward_splitkv(..., num_splits=1)): a
+    shard is a slice of a workload large enough to be spread over GPUs.
     """
     from fa import _C  # local: keeps plan_shards importable for host-only tests
 

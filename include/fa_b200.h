@@ -87,6 +87,29 @@ FA_API int fa_device_status(int32_t device, int32_t clear, uint32_t* status_out)
 /* Shared memory bytes and threads per CTA of the kernel used for (head_dim, variant). */
 FA_API int fa_kernel_info(int32_t head_dim, int32_t variant, int32_t* smem_bytes, int32_t* threads);
 
+/* ---- Split-KV (no counterpart in the reference, which lists it as not done:
+ *      docs/optimizations.md:372-373). For few heads x long N, where ceil(N / 256) * B * H
+ *      CTAs leave SMs idle, each row block's key tiles are cut into num_splits contiguous
+ *      ranges; every range writes its rows' unnormalised O and (max, sum) to a caller-owned
+ *      workspace and a second kernel merges the ranges in index order (deterministic). */
+
+/* Bytes of workspace fa_flash_fwd_splitkv needs for `params` and num_splits (1 .. 64):
+ * num_splits * batch * heads * ceil(seqlen / 256) * 256 * (head_dim + 2) * 4. */
+FA_API int fa_splitkv_workspace_size(const FaFwdParams* params, int32_t num_splits,
+                                     uint64_t* bytes_out);
+
+/* A split count for `params` on a GPU with num_sms SMs: 1 when the row blocks already fill
+ * the GPU, else about num_sms / row blocks, keeping at least two key tiles per range, at most 16. */
+FA_API int fa_splitkv_choose(const FaFwdParams* params, int32_t num_sms, int32_t* num_splits_out);
+
+/* fa_flash_fwd with the key range split num_splits ways (1 = fa_flash_fwd). `workspace`:
+ * device memory of at least fa_splitkv_workspace_size bytes, 16-byte aligned; it needs no
+ * initialisation and may be reused once the call's work on `stream` has completed. Same
+ * validation and codes as fa_flash_fwd, plus FA_ERR_INVALID_ARGUMENT for num_splits outside
+ * 1 .. 64 or a missing / small / misaligned workspace. */
+FA_API int fa_flash_fwd_splitkv(const FaFwdParams* params, int32_t num_splits, void* workspace,
+                                uint64_t workspace_bytes, fa_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

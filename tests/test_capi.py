@@ -23,7 +23,8 @@ def _declared_functions():
 
 def test_header_declares_entry_points():
     names = _declared_functions()
-    assert set(names) >= {"fa_flash_fwd", "fa_flash_fwd_sharded", "fa_last_error", "fa_device_status", "fa_kernel_info"}
+    assert set(names) >= {"fa_flash_fwd", "fa_flash_fwd_sharded", "fa_last_error", "fa_device_status", "fa_kernel_info",
+                          "fa_splitkv_workspace_size", "fa_splitkv_choose", "fa_flash_fwd_splitkv"}
 
 
 def test_library_exports_every_declared_symbol():
@@ -101,3 +102,49 @@ def test_kernel_info(d, variant):
 def test_parse_variant_message():
     with pytest.raises(RuntimeError, match="variant must be 'opt', 'fp16acc' or 'baseline', got 'x'"):
         _C.parse_variant("x")
+
+
+def test_splitkv_workspace_size_formula():
+    p = _params(batch=2, heads=3, seqlen=1000, head_dim=128)
+    out = ctypes.c_uint64(0)
+    assert _C.lib.fa_splitkv_workspace_size(ctypes.byref(p), 4, ctypes.byref(out)) == _C.FA_OK
+    rows = 1024  # ceil(1000 / 256) * 256
+    assert out.value == 4 * 6 * rows * (128 + 2) * 4
+    assert _C.lib.fa_splitkv_workspace_size(ctypes.byref(p), 1, ctypes.byref(out)) == _C.FA_OK
+    assert out.value == 0
+
+
+@pytest.mark.parametrize(
+    "b,h,n,d,variant,sms,want",
+    [
+        (4, 16, 4096, 128, 1, 148, 1),   # 1024 row blocks: no split
+        (1, 1, 16384, 128, 1, 148, 2),   # 64 row blocks
+        (1, 1, 4096, 128, 1, 148, 9),    # 16 row blocks, 32 key tiles
+        (1, 1, 1000, 64, 1, 148, 4),     # 4 row blocks, 8 key tiles: at least 2 tiles a range
+        (1, 1, 65536, 128, 1, 148, 1),   # 256 row blocks
+        (1, 1, 4096, 128, 2, 148, 4),    # fp16acc d=128: 128-row blocks (32), 32 key tiles
+        (1, 1, 100000, 64, 1, 4, 1),
+    ],
+)
+def test_splitkv_choose(b, h, n, d, variant, sms, want):
+    p = _params(batch=b, heads=h, seqlen=n, head_dim=d, variant=variant)
+    out = ctypes.c_int32(0)
+    assert _C.lib.fa_splitkv_choose(ctypes.byref(p), sms, ctypes.byref(out)) == _C.FA_OK
+    assert out.value == want
+
+
+@pytest.mark.parametrize(
+    "splits, ws, nbytes, msg",
+    [
+        (0, 0x50000, 1 << 30, "num_splits must be in 1 .. 64"),
+        (65, 0x50000, 1 << 30, "num_splits must be in 1 .. 64"),
+        (2, 0, 1 << 30, "workspace"),
+        (2, 0x50000, 16, "workspace"),
+        (2, 0x50008, 1 << 30, "16-byte aligned"),
+    ],
+)
+def test_splitkv_validation(splits, ws, nbytes, msg):
+    p = _params(seqlen=4096)
+    rc = _C.lib.fa_flash_fwd_splitkv(ctypes.byref(p), splits, ctypes.c_void_p(ws), nbytes, None)
+    assert rc == _C.FA_ERR_INVALID_ARGUMENT
+    assert msg in _C.lib.fa_last_error().decode()
