@@ -172,6 +172,36 @@ int launch_one(const FaFwdParams* p, cudaStream_t stream, int num_splits = 1,
 
 }  // namespace
 
+// Device scratch of fa_flash_fwd_splitkv_static: a fixed 32 MiB per device in the module's
+// static device memory, so that entry point allocates nothing. Its address on each device is
+// looked up once (cudaGetSymbolAddress, with that device current) and cached.
+constexpr size_t kStaticScratchBytes = size_t{32} << 20;
+static __device__ __align__(256) unsigned char g_splitkv_scratch[kStaticScratchBytes];
+
+namespace {
+
+std::mutex g_scratch_mutex;
+void* g_scratch_ptr[kMaxDevices] = {};
+
+cudaError_t scratch_ptr_for(int device, void** out) {
+    if (device < 0 || device >= kMaxDevices) {
+        return cudaErrorInvalidDevice;
+    }
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (g_scratch_ptr[device] == nullptr) {
+        void* p = nullptr;
+        const cudaError_t err = cudaGetSymbolAddress(&p, g_splitkv_scratch);
+        if (err != cudaSuccess) {
+            return err;
+        }
+        g_scratch_ptr[device] = p;
+    }
+    *out = g_scratch_ptr[device];
+    return cudaSuccess;
+}
+
+}  // namespace
+
 extern "C" {
 
 int fa_flash_fwd(const FaFwdParams* params, fa_stream_t stream) {
@@ -286,6 +316,41 @@ int fa_flash_fwd_splitkv(const FaFwdParams* params, int32_t num_splits, void* wo
                          uint64_t workspace_bytes, fa_stream_t stream) {
     return launch_one(params, reinterpret_cast<cudaStream_t>(stream), num_splits, workspace,
                       workspace_bytes);
+}
+
+int fa_flash_fwd_splitkv_static(const FaFwdParams* params, int32_t num_splits, fa_stream_t stream) {
+    const int rc = validate(params);
+    if (rc != FA_OK) {
+        return rc;
+    }
+    if (num_splits < 1 || num_splits > kMaxSplits) {
+        return fail(FA_ERR_INVALID_ARGUMENT,
+                    "flash_fwd_splitkv_static: num_splits must be in 1 .. 64, got " +
+                        std::to_string(num_splits));
+    }
+    const uint64_t need =
+        num_splits == 1 ? 0
+                        : fa_sm100::splitkv_workspace_bytes(params->batch * params->heads,
+                                                            params->seqlen, params->head_dim, num_splits);
+    if (need > kStaticScratchBytes) {
+        return fail(FA_ERR_INVALID_ARGUMENT,
+                    "flash_fwd_splitkv_static: the problem needs " + std::to_string(need) +
+                        " bytes of scratch; the static scratch holds " +
+                        std::to_string(kStaticScratchBytes) +
+                        " (use fa_flash_fwd_splitkv with a caller workspace)");
+    }
+    int device = 0;
+    cudaError_t err = cudaGetDevice(&device);
+    if (err != cudaSuccess) {
+        return cuda_fail(err, "cudaGetDevice");
+    }
+    void* scratch = nullptr;
+    err = scratch_ptr_for(device, &scratch);
+    if (err != cudaSuccess) {
+        return cuda_fail(err, "cudaGetSymbolAddress");
+    }
+    return launch_one(params, reinterpret_cast<cudaStream_t>(stream), num_splits, scratch,
+                      kStaticScratchBytes);
 }
 
 int fa_kernel_info(int32_t head_dim, int32_t variant, int32_t* smem_bytes, int32_t* threads) {

@@ -110,6 +110,19 @@ FA_API int fa_splitkv_choose(const FaFwdParams* params, int32_t num_sms, int32_t
 FA_API int fa_flash_fwd_splitkv(const FaFwdParams* params, int32_t num_splits, void* workspace,
                                 uint64_t workspace_bytes, fa_stream_t stream);
 
+/* fa_flash_fwd_splitkv without a caller workspace, allocating nothing (no counterpart in the
+ * reference). The split partials go to a fixed scratch of 32 MiB (33554432 bytes) per device,
+ * a static __device__ array of the library; a problem whose split-KV workspace
+ * (fa_splitkv_workspace_size) exceeds it is rejected with FA_ERR_INVALID_ARGUMENT and a
+ * message. Nothing in the scratch needs to start at zero: every record a call reads was
+ * written by the same call. The first call on each device looks the scratch address up
+ * (cudaGetSymbolAddress) and caches it; make that first call outside any stream capture.
+ * There is one scratch per device: calls whose work can overlap on the GPU (different streams
+ * without ordering between them) race on it and give wrong results; calls on one stream are
+ * ordered by the stream. */
+FA_API int fa_flash_fwd_splitkv_static(const FaFwdParams* params, int32_t num_splits,
+                                       fa_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
