@@ -38,10 +38,10 @@ COMMON_FLAGS = [
 ]
 
 LIBS = {
-    "libfa_b200.so": ["flash_fwd_sm100.cu", "capi.cu"],
+    "libfa_b200.so": ["flash_fwd_sm100.cu", "flash_fwd_pair_sm100.cu", "capi.cu"],
     "libfa_selftest.so": ["selftest_sm100.cu"],
 }
-HEADERS = ["sm100_ptx.cuh", "fa_internal.h", "tma_host.h"]
+HEADERS = ["sm100_ptx.cuh", "softmax_common.cuh", "fa_internal.h", "tma_host.h"]
 
 
 def nvcc_path() -> str:

@@ -101,7 +101,7 @@ int validate(const FaFwdParams* p) {
 constexpr int kMaxSplits = 64;
 
 int launch_one(const FaFwdParams* p, cudaStream_t stream, int num_splits = 1,
-               void* workspace = nullptr, uint64_t workspace_bytes = 0) {
+               void* workspace = nullptr, uint64_t workspace_bytes = 0, bool use_pair = false) {
     const int rc = validate(p);
     if (rc != FA_OK) {
         return rc;
@@ -153,7 +153,14 @@ int launch_one(const FaFwdParams* p, cudaStream_t stream, int num_splits = 1,
         args.ws_o = static_cast<float*>(workspace);
         args.ws_ml = args.ws_o + recs * p->head_dim;
     }
-    err = fa_sm100::launch_forward(prob, args, stream);
+// The CTA-pair kernel (flash_fwd_pair_sm100.cu) is correct but measured slower than the
+// one-CTA kernel on B200 (cfg3 non-causal 885 vs 1040 TFLOPS), so it is built but off.
+#ifndef FA_USE_PAIR
+#define FA_USE_PAIR 0
+#endif
+    err = ((FA_USE_PAIR || use_pair) && fa_sm100::pair_kernel_supports(prob, args))
+              ? fa_sm100::launch_forward_pair(prob, args, stream)
+              : fa_sm100::launch_forward(prob, args, stream);
     if (err == cudaErrorInvalidValue) {
         return fail(FA_ERR_CUDA, "flash_fwd: cuTensorMapEncodeTiled failed");
     }
@@ -316,6 +323,14 @@ int fa_flash_fwd_splitkv(const FaFwdParams* params, int32_t num_splits, void* wo
                          uint64_t workspace_bytes, fa_stream_t stream) {
     return launch_one(params, reinterpret_cast<cudaStream_t>(stream), num_splits, workspace,
                       workspace_bytes);
+}
+
+int fa_flash_fwd_pair(const FaFwdParams* params, fa_stream_t stream) {
+    if (params != nullptr && (params->head_dim != 128 || params->variant == FA_VARIANT_FP16ACC)) {
+        return fail(FA_ERR_INVALID_ARGUMENT,
+                    "flash_fwd_pair: head_dim 128 with the baseline or opt variant only");
+    }
+    return launch_one(params, reinterpret_cast<cudaStream_t>(stream), 1, nullptr, 0, true);
 }
 
 int fa_flash_fwd_splitkv_static(const FaFwdParams* params, int32_t num_splits, fa_stream_t stream) {

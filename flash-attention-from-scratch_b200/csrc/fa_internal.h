@@ -55,6 +55,10 @@ struct FwdProblem {
     int variant;
 };
 
+// The CTA-pair kernel (flash_fwd_pair_sm100.cu): d = 128, baseline / opt, no split-KV.
+bool pair_kernel_supports(const FwdProblem& prob, const FwdArgs& args);
+cudaError_t launch_forward_pair(const FwdProblem& prob, const FwdArgs& args, cudaStream_t stream);
+
 // Launches the split-KV combine: O[bh][row] = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s, fp16.
 cudaError_t launch_splitkv_combine(const FwdProblem& prob, const FwdArgs& args, cudaStream_t stream);
 

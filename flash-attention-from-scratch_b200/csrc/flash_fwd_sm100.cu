@@ -45,6 +45,7 @@
 
 #include "fa_internal.h"
 #include "sm100_ptx.cuh"
+#include "softmax_common.cuh"
 #include "tma_host.h"
 
 // Software-exp2 share (how many of every 8 column pairs of a 128-key tile take exp2_poly2
@@ -207,9 +208,6 @@ __device__ __forceinline__ bool trace_cta() {
     } while (0)
 #endif
 
-__device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
-__device__ __forceinline__ uint32_t f2u(float x) { return __float_as_uint(x); }
-
 // fp16 accumulator cells hold one value per 32-bit column, in the low half.
 __device__ __forceinline__ float f16cell_to_float(uint32_t cell) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(cell & 0xFFFFu)));
@@ -256,37 +254,6 @@ __device__ __forceinline__ void issue_pv_mma_f16(uint32_t tmem_t0, uint32_t tmem
                     idesc, k4 == 0 ? 0u : 1u);
         }
     }
-}
-
-// Row max (or min, for a negative scale) of N scores (N = 64 or 128): eight independent
-// three-input chains over columns 8 .. N-9, then the last eight columns.
-template <bool MAX, int N>
-__device__ __forceinline__ float row_extreme(const uint32_t (&sr)[N]) {
-    static_assert(N % 16 == 0 && N >= 32, "row_extreme covers N = 16 k columns");
-    float m[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        m[i] = u2f(sr[i]);
-    }
-#pragma unroll
-    for (int c = 8; c + 16 <= N; c += 16) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            m[i] = MAX ? fmax3(m[i], u2f(sr[c + i]), u2f(sr[c + 8 + i]))
-                       : fmin3(m[i], u2f(sr[c + i]), u2f(sr[c + 8 + i]));
-        }
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        m[i] = MAX ? fmaxf(m[i], u2f(sr[N - 8 + i])) : fminf(m[i], u2f(sr[N - 8 + i]));
-    }
-    return MAX ? fmax3(fmax3(m[0], m[1], m[2]), fmax3(m[3], m[4], m[5]), fmaxf(m[6], m[7]))
-               : fmin3(fmin3(m[0], m[1], m[2]), fmin3(m[3], m[4], m[5]), fminf(m[6], m[7]));
-}
-
-// Named barrier over the two warps (one per column half) that own the same 32 rows.
-__device__ __forceinline__ void pair_sync(int id) {
-    asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
 }
 
 template <class Cfg>

@@ -110,6 +110,13 @@ FA_API int fa_splitkv_choose(const FaFwdParams* params, int32_t num_sms, int32_t
 FA_API int fa_flash_fwd_splitkv(const FaFwdParams* params, int32_t num_splits, void* workspace,
                                 uint64_t workspace_bytes, fa_stream_t stream);
 
+/* Experimental (no counterpart in the reference): fa_flash_fwd on the CTA-pair kernel, where a
+ * cluster of two CTAs on two SMs shares each tcgen05.mma (cta_group::2) and TMEM holds two S
+ * and two P buffers, so the next scores are computed during the softmax. head_dim 128,
+ * baseline or opt variant only (FA_ERR_INVALID_ARGUMENT otherwise). Same results within the
+ * parity tolerance; measured slower than fa_flash_fwd on B200, which therefore does not use it. */
+FA_API int fa_flash_fwd_pair(const FaFwdParams* params, fa_stream_t stream);
+
 /* fa_flash_fwd_splitkv without a caller workspace, allocating nothing (no counterpart in the
  * reference). The split partials go to a fixed scratch of 32 MiB (33554432 bytes) per device,
  * a static __device__ array of the library; a problem whose split-KV workspace
