@@ -5,14 +5,16 @@
     o = fa.forward(q, k, v, fp16_accum=True)   # P.V accumulated in fp16 per 64 keys
 
 Same public surface as the reference package (fa/__init__.py:14-38): ``forward``,
-``forward_variant`` and ``attention_reference``; plus ``forward_splitkv`` and the multi-GPU
-``forward_sharded`` / ``plan_shards``. The kernel is tcgen05 / TMEM / TMA code for sm_100a in
+``forward_variant`` and ``attention_reference``; plus ``forward_splitkv``, ``forward_host`` (CPU
+tensors in and out, transfers overlapped with the kernels) and the multi-GPU ``forward_sharded`` /
+``plan_shards``. The kernel is tcgen05 / TMEM / TMA code for sm_100a in
 libfa_b200.so; there is no CPU or fallback path.
 """
 
 import torch
 
 from fa import _C
+from fa.host import forward_host
 from fa.reference import attention_reference
 from fa.shard import forward_sharded, plan_shards
 
@@ -58,5 +60,5 @@ def forward_splitkv(
     return _C.forward_splitkv(q, k, v, causal, softmax_scale, variant, num_splits)
 
 
-__all__ = ["forward", "forward_variant", "forward_splitkv", "attention_reference", "forward_sharded",
-           "plan_shards"]
+__all__ = ["forward", "forward_variant", "forward_splitkv", "forward_host", "attention_reference",
+           "forward_sharded", "plan_shards"]

@@ -54,3 +54,15 @@ def test_flops_formula():
 def test_config_table():
     assert CONFIGS["cfg1"] == dict(b=4, h=16, n=4096, d=128, causal=True, seed=1, scale=1.0)
     assert len(cfg4_cases()) == 16 and all(c["b"] * c["h"] == 256 for c in cfg4_cases())
+
+
+def test_forward_host_validates_before_touching_a_gpu():
+    import fa
+
+    q = torch.zeros(1, 1, 8, 64, dtype=torch.float16)
+    with pytest.raises(RuntimeError, match="float16"):
+        fa.forward_host(q.float(), q, q)
+    with pytest.raises(RuntimeError, match="same shape"):
+        fa.forward_host(q, q[:, :, :4].contiguous(), q)
+    with pytest.raises(RuntimeError, match="out must be"):
+        fa.forward_host(q, q, q, out=torch.zeros(1, 1, 8, 32, dtype=torch.float16))
