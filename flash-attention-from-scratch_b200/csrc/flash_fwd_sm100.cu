@@ -51,7 +51,7 @@
 // Software-exp2 share (how many of every 8 column pairs of a 128-key tile take exp2_poly2
 // instead of ex2.approx); compile-time tuning knobs.
 #ifndef FA_EMU_PER8_D128
-#define FA_EMU_PER8_D128 0
+#define FA_EMU_PER8_D128 1
 #endif
 #ifndef FA_EMU_PER8_D64
 #define FA_EMU_PER8_D64 2
@@ -65,8 +65,12 @@
 // Softmax warpgroups per query tile (fp32 variants): 2 splits the 128 columns of S between two
 // warpgroups that own the same rows and exchange row maxima through shared memory. Measured on
 // B200 at d = 128: no faster than 1 (the exponentials, not the warps' latency, bound a tile).
-#ifndef FA_EXP_POLY_DEG
-#define FA_EXP_POLY_DEG 4
+// Degree of the software 2^x polynomial per head dim (3 = the reference's cubic, 4 = ours).
+#ifndef FA_EXP_POLY_DEG_D128
+#define FA_EXP_POLY_DEG_D128 3
+#endif
+#ifndef FA_EXP_POLY_DEG_D64
+#define FA_EXP_POLY_DEG_D64 4
 #endif
 // MMA issuing threads per head dim (fp32 variants, NQ = 2): 2 gives each query tile its own
 // issuer warp, so the tensor pipe can interleave the two tiles' P.V / S MMAs. Measured on
@@ -81,6 +85,9 @@
 #endif
 #ifndef FA_MMA_ISSUERS_ACC16
 #define FA_MMA_ISSUERS_ACC16 1
+#endif
+#ifndef FA_MIXED_SUM
+#define FA_MIXED_SUM 1  // row sum via add.rn.f32.f16 instead of a conversion and a packed add
 #endif
 #ifndef FA_SPLIT_COLS
 #define FA_SPLIT_COLS 1
@@ -111,6 +118,7 @@ struct FwdCfg {
     // free once the softmax has read S_t and written P_t into the lower 64.
     static constexpr bool T_HI_IN_S = ACC16 && NQ == 2;
     static constexpr int kEmuPer8 = ACC16 ? 0 : (D == 128 ? FA_EMU_PER8_D128 : FA_EMU_PER8_D64);
+    static constexpr int kPolyDeg = (D == 128) ? FA_EXP_POLY_DEG_D128 : FA_EXP_POLY_DEG_D64;
     static constexpr int kTileBytes = kBM * D * 2;  // one Q, K, V or O tile (BM == BN)
     static constexpr int kBoxes = D / 64;           // TMA boxes per tile
     static constexpr int STAGES = (D == 128) ? 4 : 8;
@@ -499,22 +507,21 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     if constexpr (Cfg::EXP16) {
                         h = ex2_approx_f16x2(pack_half2(x2.x, x2.y));
                     } else {
-#if FA_EXP_POLY_DEG == 3
                         const float2 e = ((i % 8) < Cfg::kEmuPer8)
-                                             ? exp2_poly2_deg3(x2)
+                                             ? (Cfg::kPolyDeg == 3 ? exp2_poly2_deg3(x2) : exp2_poly2(x2))
                                              : make_float2(ex2_approx(x2.x), ex2_approx(x2.y));
-#else
-                        const float2 e = ((i % 8) < Cfg::kEmuPer8)
-                                             ? exp2_poly2(x2)
-                                             : make_float2(ex2_approx(x2.x), ex2_approx(x2.y));
-#endif
                         h = pack_half2(e.x, e.y);
                     }
                     // The row sum adds the fp16-rounded values the MMA consumes, so that O is
                     // normalised by the weights it was accumulated with. (The reference sums
                     // the fp32 values, csrc/kernels/flash_fwd.cu:403-417; measured here that
                     // is ~6% faster per tile but adds error: cfg4's outlier rows exceed 2e-3.)
+#if FA_MIXED_SUM
+                    // fp32 += fp16 with the mixed-precision add (no separate conversion).
+                    add_f16x2_to_f32(sum2[i % 4].x, sum2[i % 4].y, h);
+#else
                     sum2[i % 4] = __fadd2_rn(sum2[i % 4], unpack_half2(h));
+#endif
                     pk[i] = h;
                 }
                 tmem_st32(t_p + chunk * 32, pk);

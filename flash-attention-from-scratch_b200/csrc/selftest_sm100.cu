@@ -189,6 +189,15 @@ __global__ void exp2_probe_kernel(const float* __restrict__ x, float* __restrict
     }
 }
 
+__global__ void exp2_deg3_probe_kernel(const float* __restrict__ x, float* __restrict__ poly, int n) {
+    const int i = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
+    if (i + 1 < n) {
+        const float2 e = exp2_poly2_deg3(make_float2(x[i], x[i + 1]));
+        poly[i] = e.x;
+        poly[i + 1] = e.y;
+    }
+}
+
 // Watchdog probe: waits with the kernels' bounded wait (mbar_wait) on an mbarrier that no
 // thread ever arrives on. The wait must give up after 2^31 SM cycles, record its code in the
 // status word and let the kernel return; flags[0] = 1 if the wait reported failure, flags[1]
@@ -462,6 +471,25 @@ __attribute__((visibility("default"))) int fa_selftest_exp2(const float* x, floa
     }
     const int pairs = n / 2;
     exp2_probe_kernel<<<(pairs + 255) / 256, 256>>>(x, poly, sfu, n);
+    cudaError_t err = cudaGetLastError();
+    if (err == cudaSuccess) {
+        err = cudaDeviceSynchronize();
+    }
+    if (err != cudaSuccess) {
+        g_err = std::string("CUDA error: ") + cudaGetErrorString(err);
+        return 3;
+    }
+    return 0;
+}
+
+// exp2_poly2_deg3 (the degree-3 software 2^x) on n (even) device floats; synchronises.
+__attribute__((visibility("default"))) int fa_selftest_exp2_deg3(const float* x, float* poly, int n) {
+    using namespace fa_sm100;
+    if (n <= 0 || (n & 1) != 0) {
+        g_err = "n must be positive and even";
+        return 1;
+    }
+    exp2_deg3_probe_kernel<<<(n / 2 + 255) / 256, 256>>>(x, poly, n);
     cudaError_t err = cudaGetLastError();
     if (err == cudaSuccess) {
         err = cudaDeviceSynchronize();

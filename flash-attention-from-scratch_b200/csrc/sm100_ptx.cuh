@@ -396,6 +396,14 @@ __device__ __forceinline__ uint32_t ex2_approx_f16x2(uint32_t x) {
     return y;
 }
 
+// lo_acc += low half of h, hi_acc += high half of h (fp16 -> fp32 exactly, then an fp32 add).
+__device__ __forceinline__ void add_f16x2_to_f32(float& lo_acc, float& hi_acc, uint32_t h) {
+    asm("{\n\t.reg .b16 l, u;\n\tmov.b32 {l, u}, %2;\n\t"
+        "add.rn.f32.f16 %0, l, %0;\n\tadd.rn.f32.f16 %1, u, %1;\n\t}"
+        : "+f"(lo_acc), "+f"(hi_acc)
+        : "r"(h));
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     const __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<const uint32_t*>(&h);

@@ -89,6 +89,26 @@ def test_exp2_implementations_error_bounds():
     assert (p[~fin].half() == 0).all()
 
 
+def test_exp2_degree3_error_bound():
+    """The degree-3 software 2^x (exp2_poly2_deg3, used for 1 of 8 pairs at d = 128): max
+    relative error 1.0e-4 fitted (float32 Horner adds a little), below the 2.4e-4 worst relative
+    rounding of the fp16 value it feeds; exact at powers of two; 0 for masked scores."""
+    lib = ctypes.CDLL(str(LIB))
+    lib.fa_selftest_exp2_deg3.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+    lib.fa_selftest_error.restype = ctypes.c_char_p
+    x = torch.cat([torch.linspace(-126.0, 8.0, 1 << 20), torch.tensor([0.0, 1.0, -1.0, 8.0, float("-inf"), -200.0])]).float()
+    xd = x.cuda()
+    poly = torch.empty_like(xd)
+    assert lib.fa_selftest_exp2_deg3(xd.data_ptr(), poly.data_ptr(), xd.numel()) == 0, lib.fa_selftest_error()
+    exact = torch.exp2(x.double())
+    fin = x >= -126.0
+    rel = ((poly.cpu().double() - exact) / exact)[fin].abs().max().item()
+    assert rel < 1.2e-4, rel
+    p = poly.cpu()
+    assert p[x == 0.0].eq(1.0).all() and p[x == 1.0].eq(2.0).all() and p[x == -1.0].eq(0.5).all()
+    assert (p[~fin].half() == 0).all() and (p[~fin] >= 0).all()
+
+
 def test_bounded_wait_times_out_without_fault():
     """Failure detection on the GPU without a fault: the kernels' bounded mbarrier wait, on a
     barrier nothing arrives on, gives up after its time limit (1 s), records its code in the
