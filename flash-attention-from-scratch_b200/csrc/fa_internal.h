@@ -59,6 +59,29 @@ struct FwdProblem {
 bool pair_kernel_supports(const FwdProblem& prob, const FwdArgs& args);
 cudaError_t launch_forward_pair(const FwdProblem& prob, const FwdArgs& args, cudaStream_t stream);
 
+// Sets a kernel's dynamic shared-memory limit once per device (the attribute persists per
+// device context; setting it on every launch costs host time for nothing). Templated on the
+// kernel pointer itself, so every kernel instantiation keeps its own per-device record even when
+// several share one signature.
+template <auto Kernel>
+inline cudaError_t ensure_smem_limit(int bytes) {
+    static unsigned long long done_mask = 0;  // bit d: set on device d (benign race: idempotent)
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) {
+        return err;
+    }
+    const unsigned long long bit = (dev >= 0 && dev < 64) ? (1ull << dev) : 0ull;
+    if (bit != 0 && (__atomic_load_n(&done_mask, __ATOMIC_ACQUIRE) & bit) != 0) {
+        return cudaSuccess;
+    }
+    err = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (err == cudaSuccess && bit != 0) {
+        __atomic_fetch_or(&done_mask, bit, __ATOMIC_RELEASE);
+    }
+    return err;
+}
+
 // Launches the split-KV combine: O[bh][row] = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s, fp16.
 cudaError_t launch_splitkv_combine(const FwdProblem& prob, const FwdArgs& args, cudaStream_t stream);
 

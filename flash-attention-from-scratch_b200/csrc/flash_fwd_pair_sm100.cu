@@ -256,9 +256,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 pair_sync(pair_id);
                 continue;
             }
-            const bool tr = traced_pair && warp == 0 && lane == 0 && j < 128;
-            const bool trw = traced_pair && lane == 0 && j < 16;
-            const int wb = tbase + 512 + j * 32 + warp * 4;
+            [[maybe_unused]] const bool tr = traced_pair && warp == 0 && lane == 0 && j < 128;
+            [[maybe_unused]] const bool trw = traced_pair && lane == 0 && j < 16;
+            [[maybe_unused]] const int wb = tbase + 512 + j * 32 + warp * 4;
             PAIR_TRACE(tr, tbase + j * 4 + 0);
             PAIR_TRACE(trw, wb + 0);
             tc_fence_after();
@@ -554,7 +554,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const int k_item = next2 ? ring++ : 0;
                 const int vs = v_item % STAGES;
                 const int ks = k_item % STAGES;
-                const bool tr = traced_pair && j < 128;
+                [[maybe_unused]] const bool tr = traced_pair && j < 128;
                 ok = mbar_wait_cl(smem_u32(&sb.p_full[b]), (j >> 1) & 1, wctx, kStatusTimeoutMma);
                 PAIR_TRACE(tr, 1024 + j * 4 + 0);
                 ok = ok && mbar_wait(smem_u32(&sb.kv_full[vs]), (v_item / STAGES) & 1, wctx,
@@ -626,7 +626,7 @@ template <bool CAUSAL, int VARIANT>
 cudaError_t launch(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                    const CUtensorMap& tm_o, const FwdArgs& args, cudaStream_t stream) {
     auto* kernel = fa_fwd_pair_kernel<CAUSAL, VARIANT>;
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
+    cudaError_t err = ensure_smem_limit<fa_fwd_pair_kernel<CAUSAL, VARIANT>>(kSmemAlloc);
     if (err != cudaSuccess) {
         return err;
     }

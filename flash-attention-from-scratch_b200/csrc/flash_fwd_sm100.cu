@@ -1108,8 +1108,7 @@ cudaError_t launch_cfg(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const C
                        const CUtensorMap& tm_o, const FwdArgs& args, cudaStream_t stream) {
     using Cfg = FwdCfg<D, CAUSAL, VARIANT>;
     auto* kernel = fa_fwd_sm100_kernel<Cfg>;
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           Cfg::kSmemAlloc);
+    cudaError_t err = ensure_smem_limit<fa_fwd_sm100_kernel<Cfg>>(Cfg::kSmemAlloc);
     if (err != cudaSuccess) {
         return err;
     }

@@ -61,13 +61,13 @@ def forward_host(
         raise RuntimeError("forward_host: out must be a contiguous CPU tensor like q")
     variant = variant or ("fp16acc" if fp16_accum else "opt")
     _C.parse_variant(variant)
-    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
     b, h, n, d = (int(x) for x in q.shape)
-    if out is None:
-        out = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
     heads = b * h
     if heads == 0 or n == 0:
-        return out
+        return out if out is not None else torch.empty_like(q)
+    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    if out is None:
+        out = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
     nchunks = max(1, min(heads, chunks if chunks is not None else 8))
     bounds = [(heads * i) // nchunks for i in range(nchunks + 1)]
     qv, kv, vv, ov = (t.view(heads, 1, n, d) for t in (q, k, v, out))
