@@ -24,7 +24,9 @@
 //   Build options (measured on B200, off by default): FA_SPLIT_COLS=2 gives each query tile
 //   two softmax warpgroups that split its 128 key columns and exchange row maxima and sums
 //   through shared memory over a 64-thread named barrier; FA_REGS_SOFTMAX=R moves registers
-//   from the producer/MMA warpgroup to the softmax warpgroups (setmaxnreg).
+//   from the producer/MMA warpgroup to the softmax warpgroups (setmaxnreg); FA_PING_PONG=1
+//   makes the two tiles' softmax warps of each sub-partition take turns at the exponentials
+//   (d = 64); FA_ISSUER_SMSP_SWAP=1 moves the two d = 64 issuers to sub-partitions 0 and 3.
 //
 // Tensor memory (512 columns x 128 lanes, fp32 cells):
 //   S_t  columns [128 t, 128 t + 128)   scores of tile t, fp32
@@ -89,6 +91,18 @@
 #ifndef FA_MIXED_SUM
 #define FA_MIXED_SUM 1  // row sum via add.rn.f32.f16 instead of a conversion and a packed add
 #endif
+#ifndef FA_STAGES_D64
+#define FA_STAGES_D64 8  // K/V ring slots at d = 64 (16 KB each)
+#endif
+#ifndef FA_PING_PONG
+#define FA_PING_PONG 0  // separate P (d = 64): the two tiles take turns at the exponentials
+#endif
+#ifndef FA_ISSUER_SMSP_SWAP
+#define FA_ISSUER_SMSP_SWAP 0
+#endif
+#ifndef FA_LATE_P_WAIT
+#define FA_LATE_P_WAIT 1  // separate P columns (d = 64): wait for the previous P.V at the P store
+#endif
 #ifndef FA_SPLIT_COLS
 #define FA_SPLIT_COLS 1
 #endif
@@ -121,7 +135,8 @@ struct FwdCfg {
     static constexpr int kPolyDeg = (D == 128) ? FA_EXP_POLY_DEG_D128 : FA_EXP_POLY_DEG_D64;
     static constexpr int kTileBytes = kBM * D * 2;  // one Q, K, V or O tile (BM == BN)
     static constexpr int kBoxes = D / 64;           // TMA boxes per tile
-    static constexpr int STAGES = (D == 128) ? 4 : 8;
+    static constexpr int STAGES = (D == 128) ? 4 : FA_STAGES_D64;
+    static_assert(STAGES <= 16, "K/V ring barriers");
     // Shared memory (offsets from a 1024-byte aligned base).
     static constexpr int kSmemQ = 0;
     static constexpr int kSmemKV = NQ * kTileBytes;
@@ -143,12 +158,15 @@ struct FwdCfg {
     static constexpr int SPLIT = ACC16 ? 1 : FA_SPLIT_COLS;
     static constexpr int kCols = kBN / SPLIT;  // S columns per softmax thread
     static constexpr int kSoftmaxWarps = 4 * NQ * SPLIT;
-    static constexpr int kProducerWarp = kSoftmaxWarps;
-    static constexpr int kMmaWarp = kSoftmaxWarps + 1;
-    static constexpr int kIssuers =  // MMA issuer warps kMmaWarp + i
+    static constexpr int kIssuers =  // MMA issuer warps kMmaWarp and kIssuerWarp1
         (NQ == 2 && (ACC16 ? FA_MMA_ISSUERS_ACC16 : (D == 64 ? FA_MMA_ISSUERS_D64 : FA_MMA_ISSUERS_D128)) == 2)
             ? 2
             : 1;
+    // FA_ISSUER_SMSP_SWAP (two issuers): issuers on warps 8 + 0 and 8 + 3, producer on 8 + 1.
+    static constexpr bool kSwap = FA_ISSUER_SMSP_SWAP && kIssuers == 2;
+    static constexpr int kProducerWarp = kSoftmaxWarps + (kSwap ? 1 : 0);
+    static constexpr int kMmaWarp = kSoftmaxWarps + (kSwap ? 0 : 1);
+    static constexpr int kIssuerWarp1 = kSwap ? kSoftmaxWarps + 3 : kMmaWarp + 1;
     static constexpr int kThreads = 32 * (kSoftmaxWarps + 4);
     // Register split: every warp is launched with kRegsLaunch (65536 / threads, a multiple of
     // 8); with FA_REGS_SOFTMAX != 0 the softmax warpgroups go to that many and the
@@ -178,10 +196,11 @@ struct SharedRowStats {
     float red_sum[2][2][128];
 };
 
+constexpr int kMaxStages = 16;
 struct SharedBarriers {
     uint64_t q_full[2];
-    uint64_t kv_full[8];
-    uint64_t kv_empty[8];
+    uint64_t kv_full[kMaxStages];
+    uint64_t kv_empty[kMaxStages];
     uint64_t s_full[2];
     uint64_t s_free[2];
     uint64_t p_full[2];
@@ -199,8 +218,34 @@ struct SharedBarriers {
 // [1024, +2*4*64): MMA t: {P ready, PV issued, S(j+1) issued, V ready}
 // [2048, +256): producer ring slot: load issued
 // [2304, +2*4*64): softmax t, key tile j: arrival on P-ready of each of the tile's four warps
-// [2816, +2*4*64): fp16acc softmax t, key tile j: fold of the fp16 partials done (slot 0)
-__device__ unsigned long long g_fa_trace[4096];
+// [3328, +2*4*64): issuer t (d = 64), key tile j: {S_t(j) free, K(j+1) landed}
+// [3840, +2*4*64): softmax t, key tile j: S loaded, per warp of the tile
+// [4352, +2*4*64): ... row max done, per warp; [4864, +2*4*64): ... late P wait done, per warp
+// [2816, +2*4*64): softmax t, key tile j: {fp16acc: fold of the fp16 partials done, wait for the
+//                  previous P.V (before a rescale or a separate-P store) done}
+__device__ unsigned long long g_fa_trace[8192];
+// Per CTA (linear id < 16384): {SM clock at entry, SM clock at exit, global timer at entry,
+// global timer at exit, SM id}.
+constexpr int kCtaTraceMax = 16384;
+__device__ unsigned long long g_fa_cta_trace[kCtaTraceMax * 5];
+__device__ __forceinline__ unsigned long long global_timer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void trace_cta_time(int slot) {
+    const unsigned lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+    if (threadIdx.x == 0 && lin < kCtaTraceMax) {
+        g_fa_cta_trace[lin * 5 + slot] = clock64();
+        g_fa_cta_trace[lin * 5 + 2 + slot] = global_timer_ns();
+        if (slot == 0) {
+            unsigned sm;
+            asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+            g_fa_cta_trace[lin * 5 + 4] = sm;
+        }
+    }
+}
+#define FA_TRACE_CTA(slot) trace_cta_time(slot)
 __device__ __forceinline__ bool trace_cta() {
     return blockIdx.x == gridDim.x / 2 && blockIdx.y == 0;
 }
@@ -213,6 +258,9 @@ __device__ __forceinline__ bool trace_cta() {
 #else
 #define FA_TRACE_AT(idx) \
     do {                 \
+    } while (0)
+#define FA_TRACE_CTA(slot) \
+    do {                   \
     } while (0)
 #endif
 
@@ -278,6 +326,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     __shared__ SharedBarriers sb;
     __shared__ SharedRowStats rs;
 
+    FA_TRACE_CTA(0);
     const int warp = static_cast<int>(threadIdx.x) / 32;
     const int lane = static_cast<int>(threadIdx.x) % 32;
 
@@ -402,14 +451,43 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         float row_sum = 0.0f;       // running sum of this thread's fp16-rounded probabilities
         bool ok = true;
 
+        // Exponential ping-pong (separate P, d = 64): the two query tiles' warps on one SM
+        // sub-partition (warps q and q + 4) take turns at the exponential loop, so that one
+        // tile's exponentials run while the other loads S, reduces its max or waits, instead of
+        // both sharing the sub-partition's exponential unit at once. Warp q of tile t waits on
+        // barrier pp_bar(q, t) and releases the other tile's; tile 0 goes first (tile 1 releases
+        // it once before its loop). Both tiles take turns for the first min(n_kv[0], n_kv[1])
+        // key tiles only, and every path through an iteration passes the same barriers, so
+        // the arrivals and waits on each barrier always pair up.
+        constexpr bool kPingPong = Cfg::SEP_P && SPLIT == 1 && NQ == 2 && FA_PING_PONG;
+        const int pp_turns = kPingPong ? min(n_kv[0], n_kv[NQ - 1]) : 0;
+        const int pp_mine = 1 + (warp % 4) * 2 + t;
+        const int pp_other = 1 + (warp % 4) * 2 + (t ^ 1);
+        auto pp_enter = [&](int j) {
+            if (kPingPong && j < pp_turns) {
+                named_bar_sync(pp_mine, 64);
+            }
+        };
+        auto pp_leave = [&](int j) {
+            if (kPingPong && j < pp_turns && !(t == 1 && j == pp_turns - 1)) {
+                named_bar_arrive(pp_other, 64);
+            }
+        };
+        if (kPingPong && t == 1 && pp_turns > 0) {
+            named_bar_arrive(pp_other, 64);
+        }
+
         // A warp that gave up on a wait keeps iterating without touching TMEM, so that the two
-        // column halves of a row always pass the same number of pair barriers.
+        // column halves of a row always pass the same number of pair barriers (and the two
+        // tiles the same number of ping-pong barriers).
         for (int j = 0; j < nt; ++j) {
             ok = ok && __all_sync(0xffffffffu, mbar_wait(bar_s, j & 1, wctx, kStatusTimeoutSoftmax));
             if (!ok) {
                 if constexpr (SPLIT == 2) {
                     pair_sync(pair_id);
                 }
+                pp_enter(j);
+                pp_leave(j);
                 continue;
             }
             if (row == 0 && half == 0 && j < 64) {
@@ -424,6 +502,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             tmem_wait_ld();
             if (row == 0 && half == 0 && j < 64) {
                 FA_TRACE_AT((t * 64 + j) * 4 + 1);
+            }
+            if (lane == 0 && half == 0 && j < 64) {
+                FA_TRACE_AT(3840 + (t * 64 + j) * 4 + (warp % 4));
             }
             if constexpr (Cfg::SEP_P) {
                 // S_t is in registers: the MMA warp may overwrite it with S_t(j+1).
@@ -469,6 +550,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             if (row == 0 && half == 0 && j < 64) {
                 FA_TRACE_AT((t * 64 + j) * 4 + 3);
             }
+            if (lane == 0 && half == 0 && j < 64) {
+                FA_TRACE_AT(4352 + (t * 64 + j) * 4 + (warp % 4));
+            }
             // Running max update (lazy for "opt": keep the old max unless it grew by > 2^8).
             const float new_max = (tile_max > row_max + Cfg::kRescaleThreshold) ? tile_max : row_max;
             const float max_used = (new_max == -INFINITY) ? 0.0f : new_max;
@@ -479,13 +563,21 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             // P_t(j-1) (d = 64: in its own columns) must have been consumed before P_t(j) is
             // written; O must hold P.V up to tile j-1 before it is rescaled.
             const bool need_rescale = (!Cfg::ACC16) && j > 0 && (__any_sync(0xffffffffu, grew) != 0);
-            if ((Cfg::SEP_P && j > 0) || need_rescale) {
+            // With P in its own columns the wait is deferred to the first P store (below), so
+            // the exponentials of the first chunk overlap the previous P.V.
+            constexpr bool kLateWait = Cfg::SEP_P && FA_LATE_P_WAIT;
+            if (!kLateWait && ((Cfg::SEP_P && j > 0) || need_rescale)) {
                 ok = __all_sync(0xffffffffu,
                                 mbar_wait(bar_o, (j - 1) & 1, wctx, kStatusTimeoutSoftmax));
                 if (!ok) {
+                    pp_enter(j);
+                    pp_leave(j);
                     continue;
                 }
                 tc_fence_after();
+                if (row == 0 && half == 0 && j < 64) {
+                    FA_TRACE_AT(2816 + (t * 64 + j) * 4 + 1);
+                }
             }
 
             // Probabilities, packed fp16 pairs, into P_t.
@@ -496,6 +588,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             for (int i = 0; i < 4; ++i) {
                 sum2[i] = make_float2(0.0f, 0.0f);
             }
+            pp_enter(j);
 #pragma unroll
             for (int chunk = 0; chunk < NC / 64; ++chunk) {
                 uint32_t pk[32];
@@ -524,7 +617,27 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 #endif
                     pk[i] = h;
                 }
-                tmem_st32(t_p + chunk * 32, pk);
+                if (kLateWait && chunk == 0 && j > 0) {
+                    // P_t(j-1) consumed and O up to date (needed by the rescale below as well).
+                    ok = __all_sync(0xffffffffu,
+                                    mbar_wait(bar_o, (j - 1) & 1, wctx, kStatusTimeoutSoftmax));
+                    if (ok) {
+                        tc_fence_after();
+                        if (row == 0 && half == 0 && j < 64) {
+                            FA_TRACE_AT(2816 + (t * 64 + j) * 4 + 1);
+                        }
+                        if (lane == 0 && half == 0 && j < 64) {
+                            FA_TRACE_AT(4864 + (t * 64 + j) * 4 + (warp % 4));
+                        }
+                    }
+                }
+                if (ok) {
+                    tmem_st32(t_p + chunk * 32, pk);
+                }
+            }
+            pp_leave(j);
+            if (!ok) {
+                continue;
             }
             const float2 s01 = __fadd2_rn(sum2[0], sum2[1]);
             const float2 s23 = __fadd2_rn(sum2[2], sum2[3]);
@@ -768,14 +881,14 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             }
         }
         __syncwarp();
-    } else if (Cfg::kIssuers == 2 && warp >= Cfg::kMmaWarp && warp < Cfg::kMmaWarp + 2) {
+    } else if (Cfg::kIssuers == 2 && (warp == Cfg::kMmaWarp || warp == Cfg::kIssuerWarp1)) {
         // =========================== MMA issuers, one per query tile ===========================
         // Issuer t walks the whole K/V ring (so that each slot's release takes one arrival per
         // issuer) and issues only tile t's MMAs. It waits for every slot to land before it
         // releases it, even one its tile does not read, so it can never release a later use
         // of a slot before the producer has filled the current one.
         if (lane == 0) {
-            const int t = warp - Cfg::kMmaWarp;
+            const int t = (warp == Cfg::kMmaWarp) ? 0 : 1;
             bool ok = true;
             if (n_kv[t] > 0) {
                 ok = mbar_wait(smem_u32(&sb.q_full[t]), 0, wctx, kStatusTimeoutMma);
@@ -816,11 +929,17 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     if constexpr (Cfg::SEP_P) {
                         // S_t(j+1) as soon as the softmax has S_t(j) in registers.
                         if (next_s) {
-                            ok = mbar_wait(smem_u32(&sb.s_free[t]), j & 1, wctx, kStatusTimeoutMma) &&
-                                 mbar_wait(smem_u32(&sb.kv_full[ks]), (k_slot / STAGES) & 1, wctx,
-                                           kStatusTimeoutMma);
+                            ok = mbar_wait(smem_u32(&sb.s_free[t]), j & 1, wctx, kStatusTimeoutMma);
+                            if (j < 64) {
+                                FA_TRACE_AT(3328 + (t * 64 + j) * 4 + 0);
+                            }
+                            ok = ok && mbar_wait(smem_u32(&sb.kv_full[ks]), (k_slot / STAGES) & 1, wctx,
+                                                 kStatusTimeoutMma);
                             if (!ok) {
                                 break;
+                            }
+                            if (j < 64) {
+                                FA_TRACE_AT(3328 + (t * 64 + j) * 4 + 1);
                             }
                             k_ready = true;
                             tc_fence_after();
@@ -1037,6 +1156,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem, Cfg::kTmemCols);
     }
+    FA_TRACE_CTA(1);
 }
 
 // Split-KV combine (reference: none; Flash-Decoding's merge of per-range softmax partials).
@@ -1222,14 +1342,25 @@ int kernel_rows_per_cta(int head_dim, int variant) {
 
 #ifdef FA_TRACE
 int trace_read(unsigned long long* out, int n) {
-    if (n > 4096) {
-        n = 4096;
+    if (n > 8192) {
+        n = 8192;
     }
     return cudaMemcpyFromSymbol(out, g_fa_trace, sizeof(unsigned long long) * n) == cudaSuccess ? n : -1;
 }
 int trace_clear() {
-    static unsigned long long zero[4096] = {};
-    return cudaMemcpyToSymbol(g_fa_trace, zero, sizeof(zero)) == cudaSuccess ? 0 : -1;
+    static unsigned long long zero[kCtaTraceMax * 5] = {};
+    if (cudaMemcpyToSymbol(g_fa_cta_trace, zero, sizeof(zero)) != cudaSuccess) {
+        return -1;
+    }
+    return cudaMemcpyToSymbol(g_fa_trace, zero, sizeof(unsigned long long) * 8192) == cudaSuccess ? 0 : -1;
+}
+int trace_cta_read(unsigned long long* out, int n_cta) {
+    if (n_cta > kCtaTraceMax) {
+        n_cta = kCtaTraceMax;
+    }
+    return cudaMemcpyFromSymbol(out, g_fa_cta_trace, sizeof(unsigned long long) * 5 * n_cta) == cudaSuccess
+               ? n_cta
+               : -1;
 }
 #endif
 
@@ -1241,5 +1372,8 @@ extern "C" __attribute__((visibility("default"))) int fa_trace_read(unsigned lon
 }
 extern "C" __attribute__((visibility("default"))) int fa_trace_clear(void) {
     return fa_sm100::trace_clear();
+}
+extern "C" __attribute__((visibility("default"))) int fa_trace_cta_read(unsigned long long* out, int n_cta) {
+    return fa_sm100::trace_cta_read(out, n_cta);
 }
 #endif

@@ -77,6 +77,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return done != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete sleeps until the phase
+// completes or about `hint_ns` pass, instead of returning after the system's default limit, so
+// that a waiting warp takes fewer issue slots from the warps sharing its sub-partition.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return done != 0;
+}
+
+#ifndef FA_WAIT_SUSPEND_NS
+#define FA_WAIT_SUSPEND_NS 0  // 0: default try_wait limit
+#endif
+
 // Where a bounded wait reports that it gave up.
 struct WaitCtx {
     volatile int* cta_abort;           // shared flag: some thread of this CTA gave up
@@ -101,7 +120,8 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const W
     const long long t0 = clock64();
     uint32_t spins = 0;
     while (true) {
-        if (mbar_try_wait(bar, parity)) {
+        if (FA_WAIT_SUSPEND_NS > 0 ? mbar_try_wait_sleep(bar, parity, FA_WAIT_SUSPEND_NS)
+                                   : mbar_try_wait(bar, parity)) {
             return true;
         }
         // The abort flag and the clock are checked every 32 polls only: a polling warp shares

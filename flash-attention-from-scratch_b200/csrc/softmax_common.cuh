@@ -37,6 +37,14 @@ __device__ __forceinline__ float row_extreme(const uint32_t (&sr)[N]) {
                : fmin3(fmin3(m[0], m[1], m[2]), fmin3(m[3], m[4], m[5]), fminf(m[6], m[7]));
 }
 
+// Named barrier `id` over `n` threads: wait (bar.sync) / signal without waiting (bar.arrive).
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void named_bar_arrive(int id, int n) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
 // Named barrier over the two warps (one per column half) that own the same 32 rows.
 __device__ __forceinline__ void pair_sync(int id) {
     asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
