@@ -30,6 +30,8 @@ struct FwdArgs {
     int rows_pad;         // workspace rows per head: ceil(N / 256) * 256
     float* ws_o;          // [num_splits][num_bh][rows_pad][D] fp32
     float* ws_ml;         // [num_splits][num_bh][rows_pad][2] fp32: m (log2 units), l
+    int num_items;        // work items (row blocks x heads x key ranges), set by the launcher
+    void* o;              // output [num_bh][seqlen][D] fp16, set by the launcher
 };
 
 // Split-KV workspace bytes for a problem (16-byte aligned sections).
