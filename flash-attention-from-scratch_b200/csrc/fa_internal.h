@@ -23,9 +23,9 @@ struct FwdArgs {
     unsigned epoch;       // launch epoch, never 0
     DeviceStatus* status; // per-device watchdog record
     int head_group;       // causal schedule: heads interleaved in one heavy-first sweep (>= 1)
-    // Split-KV (num_splits > 1): CTA (x, y, z) covers the z-th of num_splits contiguous
-    // ranges of its row block's key tiles and writes, per row, its unnormalised fp32 O and
-    // (m, l) to the workspace instead of O; a combine kernel merges the splits.
+    // Split-KV (num_splits > 1): the work item of key range z covers the z-th of num_splits
+    // contiguous ranges of its row block's key tiles and writes, per row, its unnormalised fp32
+    // O and (m, l) to the workspace instead of O; a combine kernel merges the ranges.
     int num_splits;       // 1 = no split
     int rows_pad;         // workspace rows per head: ceil(N / 256) * 256
     float* ws_o;          // [num_splits][num_bh][rows_pad][D] fp32
