@@ -1,6 +1,6 @@
 """Compiles the reference's CUDA kernel, unmodified, for sm_100a (a context line for bench.py).
 
-    python baseline/build_ref_kernel.py [--reference DIR]
+    python baseline/build_ref_kernel.py REFERENCE_DIR      (or FA_REFERENCE_DIR=REFERENCE_DIR)
 
 Sources are read where they lie in the reference checkout (csrc/kernels/flash_fwd.cu with
 csrc/common.cuh and csrc/flash_fwd.h); nothing is copied into this repository. The flags are the
@@ -11,7 +11,7 @@ reference's own nvcc flags (setup.py:12-18: -O3 -std=c++20 --use_fast_math -line
 
 from __future__ import annotations
 
-import argparse
+import hashlib
 import os
 import shutil
 import subprocess
@@ -20,10 +20,14 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref" / "libfa_ref_kernel.so"
-DEFAULT_REFERENCE = Path("/root/reference")
 
 
-def build(reference: Path = DEFAULT_REFERENCE, quiet: bool = False) -> Path | None:
+def build(reference: Path | None, quiet: bool = False) -> Path | None:
+    """Builds OUT from `reference` (a checkout of the reference); returns None when its kernel
+    source is not there."""
+    if reference is None:
+        return None
+    reference = Path(reference)
     kernel = reference / "csrc" / "kernels" / "flash_fwd.cu"
     if not kernel.exists():
         if not quiet:
@@ -32,14 +36,20 @@ def build(reference: Path = DEFAULT_REFERENCE, quiet: bool = False) -> Path | No
     nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
     OUT.parent.mkdir(parents=True, exist_ok=True)
     deps = [kernel, reference / "csrc" / "common.cuh", reference / "csrc" / "flash_fwd.h",
-            HERE / "ref_kernel_shim.cu", Path(__file__)]
-    if OUT.exists() and all(d.stat().st_mtime <= OUT.stat().st_mtime for d in deps):
+            HERE / "ref_kernel_shim.cu"]
+    flags = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++20",
+             "--use_fast_math", "-lineinfo", "--expt-relaxed-constexpr",
+             "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden", "-shared"]
+    h = hashlib.sha256("\0".join(flags).encode())
+    for d in deps:
+        h.update(b"\0" + d.read_bytes())
+    digest = h.hexdigest()
+    stamp = OUT.with_name(OUT.name + ".stamp")
+    if OUT.exists() and stamp.exists() and stamp.read_text().strip() == digest:
         return OUT
     tmp = OUT.with_suffix(".so.tmp")
-    cmd = [nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++20",
-           "--use_fast_math", "-lineinfo", "--expt-relaxed-constexpr",
-           "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden", "-shared",
-           "-I", str(reference / "csrc"), "-o", str(tmp), str(kernel), str(HERE / "ref_kernel_shim.cu")]
+    cmd = [nvcc, *flags, "-I", str(reference / "csrc"), "-o", str(tmp), str(kernel),
+           str(HERE / "ref_kernel_shim.cu")]
     if not quiet:
         print("[build_ref_kernel]", " ".join(cmd), flush=True)
     res = subprocess.run(cmd, capture_output=True, text=True)
@@ -47,14 +57,15 @@ def build(reference: Path = DEFAULT_REFERENCE, quiet: bool = False) -> Path | No
         sys.stderr.write(res.stdout + res.stderr)
         raise RuntimeError("nvcc failed building the reference kernel")
     os.replace(tmp, OUT)
+    stamp.write_text(digest + "\n")
     return OUT
 
 
 def main() -> None:
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", type=Path, default=DEFAULT_REFERENCE)
-    a = ap.parse_args()
-    print("built", build(a.reference))
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FA_REFERENCE_DIR")
+    if ref is None:
+        raise SystemExit("usage: python baseline/build_ref_kernel.py REFERENCE_DIR (or set FA_REFERENCE_DIR)")
+    print("built", build(Path(ref)))
 
 
 if __name__ == "__main__":

@@ -13,6 +13,7 @@ same -O3 -lineinfo spirit, but a fixed sm_100a target and a plain shared library
 from __future__ import annotations
 
 import argparse
+import hashlib
 import os
 import shutil
 import subprocess
@@ -38,10 +39,10 @@ COMMON_FLAGS = [
 ]
 
 LIBS = {
-    "libfa_b200.so": ["flash_fwd_sm100.cu", "flash_fwd_pair_sm100.cu", "capi.cu"],
+    "libfa_b200.so": ["flash_fwd_sm100.cu", "capi.cu", "capi_static.cu"],
     "libfa_selftest.so": ["selftest_sm100.cu"],
 }
-HEADERS = ["sm100_ptx.cuh", "softmax_common.cuh", "fa_internal.h", "tma_host.h"]
+HEADERS = ["sm100_ptx.cuh", "softmax_common.cuh", "fa_internal.h", "tma_host.h", "capi_internal.h"]
 
 
 def nvcc_path() -> str:
@@ -51,25 +52,41 @@ def nvcc_path() -> str:
     raise RuntimeError("nvcc not found")
 
 
-def _stale(target: Path, sources: list[Path]) -> bool:
-    if not target.exists():
-        return True
-    t = target.stat().st_mtime
-    return any(s.stat().st_mtime > t for s in sources)
+def _digest(files: list[Path], cmd: list[str]) -> str:
+    """SHA-256 over the compile command and the bytes of every input file."""
+    h = hashlib.sha256()
+    h.update("\0".join(cmd).encode())
+    for f in files:
+        h.update(b"\0" + f.name.encode() + b"\0")
+        h.update(f.read_bytes())
+    return h.hexdigest()
+
+
+def _stamp(target: Path) -> Path:
+    return target.with_name(target.name + ".stamp")
+
+
+def _up_to_date(target: Path, digest: str) -> bool:
+    """True when `target` exists and was built from exactly these inputs (its stamp holds their
+    digest); a prebuilt library from other sources is rebuilt whatever its timestamps."""
+    stamp = _stamp(target)
+    return target.exists() and stamp.exists() and stamp.read_text().strip() == digest
 
 
 def build(force: bool = False, verbose_ptxas: bool = False, quiet: bool = False) -> list[Path]:
     nvcc = nvcc_path()
     built = []
-    deps = [CSRC / h for h in HEADERS] + [INCLUDE / "fa_b200.h", Path(__file__)]
+    deps = [CSRC / h for h in HEADERS] + [INCLUDE / "fa_b200.h"]
     for lib, srcs in LIBS.items():
         target = OUT_DIR / lib
         sources = [CSRC / s for s in srcs]
-        if not force and not _stale(target, sources + deps):
+        flags = [*ARCH_FLAGS, *COMMON_FLAGS]
+        digest = _digest(sources + deps, flags + srcs)
+        if not force and _up_to_date(target, digest):
             built.append(target)
             continue
         tmp = target.with_suffix(".so.tmp")
-        cmd = [nvcc, *ARCH_FLAGS, *COMMON_FLAGS, "-I", str(CSRC), "-I", str(INCLUDE)]
+        cmd = [nvcc, *flags, "-I", str(CSRC), "-I", str(INCLUDE)]
         if verbose_ptxas:
             cmd += ["-Xptxas", "-v"]
         # Export the C ABI (default visibility) while hiding everything else.
@@ -85,6 +102,7 @@ def build(force: bool = False, verbose_ptxas: bool = False, quiet: bool = False)
             if out:
                 print(out)
         os.replace(tmp, target)
+        _stamp(target).write_text(digest + "\n")
         built.append(target)
     return built
 

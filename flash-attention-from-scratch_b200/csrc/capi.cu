@@ -17,16 +17,23 @@
 #include <string>
 
 #include "../../include/fa_b200.h"
+#include "capi_internal.h"
 #include "fa_internal.h"
 
-namespace {
+namespace fa_capi {
 
+namespace {
 thread_local std::string g_last_error;
+}  // namespace
 
 int fail(int code, const std::string& msg) {
     g_last_error = msg;
     return code;
 }
+
+void clear_error() { g_last_error.clear(); }
+
+const char* last_error() { return g_last_error.c_str(); }
 
 int cuda_fail(cudaError_t err, const char* what) {
     return fail(FA_ERR_CUDA, std::string("flash_fwd: CUDA error in ") + what + ": " +
@@ -35,30 +42,22 @@ int cuda_fail(cudaError_t err, const char* what) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// One watchdog record per device, a file-scope __device__ variable; its address on each device
-// is looked up once (with that device current) and cached.
+namespace {
+
+// One watchdog record per device, a file-scope __device__ variable; its address is looked up
+// with the device current and cached for the device's current context.
 __device__ fa_sm100::DeviceStatus g_device_status;
 
-constexpr int kMaxDevices = 64;
-std::mutex g_status_mutex;
-fa_sm100::DeviceStatus* g_status_ptr[kMaxDevices] = {};
+SymbolCache g_status_cache;
 std::atomic<unsigned> g_epoch{0};
 
 cudaError_t status_ptr_for(int device, fa_sm100::DeviceStatus** out) {
-    if (device < 0 || device >= kMaxDevices) {
-        return cudaErrorInvalidDevice;
-    }
-    std::lock_guard<std::mutex> lock(g_status_mutex);
-    if (g_status_ptr[device] == nullptr) {
-        void* p = nullptr;
-        const cudaError_t err = cudaGetSymbolAddress(&p, g_device_status);
-        if (err != cudaSuccess) {
-            return err;
-        }
-        g_status_ptr[device] = static_cast<fa_sm100::DeviceStatus*>(p);
-    }
-    *out = g_status_ptr[device];
-    return cudaSuccess;
+    void* p = nullptr;
+    const cudaError_t err = g_status_cache.get(device, &p, [](void** dst) {
+        return cudaGetSymbolAddress(dst, g_device_status);
+    });
+    *out = static_cast<fa_sm100::DeviceStatus*>(p);
+    return err;
 }
 
 unsigned next_epoch() {
@@ -68,6 +67,8 @@ unsigned next_epoch() {
     }
     return e;
 }
+
+}  // namespace
 
 int validate(const FaFwdParams* p) {
     if (p == nullptr) {
@@ -98,10 +99,8 @@ int validate(const FaFwdParams* p) {
     return FA_OK;
 }
 
-constexpr int kMaxSplits = 64;
-
-int launch_one(const FaFwdParams* p, cudaStream_t stream, int num_splits = 1,
-               void* workspace = nullptr, uint64_t workspace_bytes = 0, bool use_pair = false) {
+int launch_one(const FaFwdParams* p, cudaStream_t stream, int num_splits, void* workspace,
+               uint64_t workspace_bytes) {
     const int rc = validate(p);
     if (rc != FA_OK) {
         return rc;
@@ -153,14 +152,7 @@ int launch_one(const FaFwdParams* p, cudaStream_t stream, int num_splits = 1,
         args.ws_o = static_cast<float*>(workspace);
         args.ws_ml = args.ws_o + recs * p->head_dim;
     }
-// The CTA-pair kernel (flash_fwd_pair_sm100.cu) is correct but measured slower than the
-// one-CTA kernel on B200 (cfg3 non-causal 885 vs 1040 TFLOPS), so it is built but off.
-#ifndef FA_USE_PAIR
-#define FA_USE_PAIR 0
-#endif
-    err = ((FA_USE_PAIR || use_pair) && fa_sm100::pair_kernel_supports(prob, args))
-              ? fa_sm100::launch_forward_pair(prob, args, stream)
-              : fa_sm100::launch_forward(prob, args, stream);
+    err = fa_sm100::launch_forward(prob, args, stream);
     if (err == cudaErrorInvalidValue) {
         return fail(FA_ERR_CUDA, "flash_fwd: cuTensorMapEncodeTiled failed");
     }
@@ -173,46 +165,21 @@ int launch_one(const FaFwdParams* p, cudaStream_t stream, int num_splits = 1,
             return cuda_fail(err, "split-KV combine launch");
         }
     }
-    g_last_error.clear();
+    clear_error();
     return FA_OK;
 }
 
-}  // namespace
+}  // namespace fa_capi
 
-// Device scratch of fa_flash_fwd_splitkv_static: a fixed 32 MiB per device in the module's
-// static device memory, so that entry point allocates nothing. Its address on each device is
-// looked up once (cudaGetSymbolAddress, with that device current) and cached.
-constexpr size_t kStaticScratchBytes = size_t{32} << 20;
-static __device__ __align__(256) unsigned char g_splitkv_scratch[kStaticScratchBytes];
-
-namespace {
-
-std::mutex g_scratch_mutex;
-void* g_scratch_ptr[kMaxDevices] = {};
-
-cudaError_t scratch_ptr_for(int device, void** out) {
-    if (device < 0 || device >= kMaxDevices) {
-        return cudaErrorInvalidDevice;
-    }
-    std::lock_guard<std::mutex> lock(g_scratch_mutex);
-    if (g_scratch_ptr[device] == nullptr) {
-        void* p = nullptr;
-        const cudaError_t err = cudaGetSymbolAddress(&p, g_splitkv_scratch);
-        if (err != cudaSuccess) {
-            return err;
-        }
-        g_scratch_ptr[device] = p;
-    }
-    *out = g_scratch_ptr[device];
-    return cudaSuccess;
-}
-
-}  // namespace
+using fa_capi::cuda_fail;
+using fa_capi::fail;
+using fa_capi::launch_one;
+using fa_capi::validate;
 
 extern "C" {
 
 int fa_flash_fwd(const FaFwdParams* params, fa_stream_t stream) {
-    return launch_one(params, reinterpret_cast<cudaStream_t>(stream));
+    return launch_one(params, reinterpret_cast<cudaStream_t>(stream), 1, nullptr, 0);
 }
 
 int fa_flash_fwd_sharded(const FaFwdParams* shards, const int32_t* devices,
@@ -233,13 +200,14 @@ int fa_flash_fwd_sharded(const FaFwdParams* shards, const int32_t* devices,
             break;
         }
         rc = launch_one(&shards[i],
-                        streams != nullptr ? reinterpret_cast<cudaStream_t>(streams[i]) : nullptr);
+                        streams != nullptr ? reinterpret_cast<cudaStream_t>(streams[i]) : nullptr, 1,
+                        nullptr, 0);
     }
     cudaSetDevice(prev);
     return rc;
 }
 
-const char* fa_last_error(void) { return g_last_error.c_str(); }
+const char* fa_last_error(void) { return fa_capi::last_error(); }
 
 int fa_device_status(int32_t device, int32_t clear, uint32_t* status_out) {
     int prev = 0;
@@ -253,7 +221,7 @@ int fa_device_status(int32_t device, int32_t clear, uint32_t* status_out) {
     }
     fa_sm100::DeviceStatus* ptr = nullptr;
     fa_sm100::DeviceStatus host{};
-    err = status_ptr_for(device, &ptr);
+    err = fa_capi::status_ptr_for(device, &ptr);
     if (err == cudaSuccess) {
         err = cudaDeviceSynchronize();
     }
@@ -279,7 +247,7 @@ int fa_splitkv_workspace_size(const FaFwdParams* params, int32_t num_splits, uin
     if (rc != FA_OK) {
         return rc;
     }
-    if (num_splits < 1 || num_splits > kMaxSplits) {
+    if (num_splits < 1 || num_splits > fa_capi::kMaxSplits) {
         return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd_splitkv: num_splits must be in 1 .. 64, got " +
                                                  std::to_string(num_splits));
     }
@@ -289,7 +257,7 @@ int fa_splitkv_workspace_size(const FaFwdParams* params, int32_t num_splits, uin
                                                                          params->seqlen, params->head_dim,
                                                                          num_splits);
     }
-    g_last_error.clear();
+    fa_capi::clear_error();
     return FA_OK;
 }
 
@@ -315,7 +283,7 @@ int fa_splitkv_choose(const FaFwdParams* params, int32_t num_sms, int32_t* num_s
     if (num_splits_out != nullptr) {
         *num_splits_out = splits;
     }
-    g_last_error.clear();
+    fa_capi::clear_error();
     return FA_OK;
 }
 
@@ -323,49 +291,6 @@ int fa_flash_fwd_splitkv(const FaFwdParams* params, int32_t num_splits, void* wo
                          uint64_t workspace_bytes, fa_stream_t stream) {
     return launch_one(params, reinterpret_cast<cudaStream_t>(stream), num_splits, workspace,
                       workspace_bytes);
-}
-
-int fa_flash_fwd_pair(const FaFwdParams* params, fa_stream_t stream) {
-    if (params != nullptr && (params->head_dim != 128 || params->variant == FA_VARIANT_FP16ACC)) {
-        return fail(FA_ERR_INVALID_ARGUMENT,
-                    "flash_fwd_pair: head_dim 128 with the baseline or opt variant only");
-    }
-    return launch_one(params, reinterpret_cast<cudaStream_t>(stream), 1, nullptr, 0, true);
-}
-
-int fa_flash_fwd_splitkv_static(const FaFwdParams* params, int32_t num_splits, fa_stream_t stream) {
-    const int rc = validate(params);
-    if (rc != FA_OK) {
-        return rc;
-    }
-    if (num_splits < 1 || num_splits > kMaxSplits) {
-        return fail(FA_ERR_INVALID_ARGUMENT,
-                    "flash_fwd_splitkv_static: num_splits must be in 1 .. 64, got " +
-                        std::to_string(num_splits));
-    }
-    const uint64_t need =
-        num_splits == 1 ? 0
-                        : fa_sm100::splitkv_workspace_bytes(params->batch * params->heads,
-                                                            params->seqlen, params->head_dim, num_splits);
-    if (need > kStaticScratchBytes) {
-        return fail(FA_ERR_INVALID_ARGUMENT,
-                    "flash_fwd_splitkv_static: the problem needs " + std::to_string(need) +
-                        " bytes of scratch; the static scratch holds " +
-                        std::to_string(kStaticScratchBytes) +
-                        " (use fa_flash_fwd_splitkv with a caller workspace)");
-    }
-    int device = 0;
-    cudaError_t err = cudaGetDevice(&device);
-    if (err != cudaSuccess) {
-        return cuda_fail(err, "cudaGetDevice");
-    }
-    void* scratch = nullptr;
-    err = scratch_ptr_for(device, &scratch);
-    if (err != cudaSuccess) {
-        return cuda_fail(err, "cudaGetSymbolAddress");
-    }
-    return launch_one(params, reinterpret_cast<cudaStream_t>(stream), num_splits, scratch,
-                      kStaticScratchBytes);
 }
 
 int fa_kernel_info(int32_t head_dim, int32_t variant, int32_t* smem_bytes, int32_t* threads) {

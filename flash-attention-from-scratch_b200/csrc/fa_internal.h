@@ -2,8 +2,11 @@
 // Host/device shared definitions of the sm_100a forward kernel (torch-free).
 
 #include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
+
 #include <cstdint>
+#include <mutex>
 
 namespace fa_sm100 {
 
@@ -57,29 +60,60 @@ struct FwdProblem {
     int variant;
 };
 
-// The CTA-pair kernel (flash_fwd_pair_sm100.cu): d = 128, baseline / opt, no split-KV.
-bool pair_kernel_supports(const FwdProblem& prob, const FwdArgs& args);
-cudaError_t launch_forward_pair(const FwdProblem& prob, const FwdArgs& args, cudaStream_t stream);
+// Unique id (cuCtxGetId, plus one) of the calling thread's current CUDA context, or 0 when
+// no context is current or the driver lacks the call. Values the library caches per device
+// (device addresses of module variables, kernel attributes that were set) belong to one
+// context: a device reset destroys the primary context and a new one replaces it, so every
+// such cache keys its entries on this id and refills them when it changes.
+inline unsigned long long current_context_id() {
+    static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
+    static PFN_cuCtxGetId_v12000 get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 4000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) {
+            get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+        }
+        p = nullptr;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) {
+            get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(p);
+        }
+    });
+    CUcontext ctx = nullptr;
+    if (get_current == nullptr || get_id == nullptr || get_current(&ctx) != CUDA_SUCCESS ||
+        ctx == nullptr) {
+        return 0;
+    }
+    unsigned long long id = 0;
+    return get_id(ctx, &id) == CUDA_SUCCESS ? id + 1 : 0;
+}
 
-// Sets a kernel's dynamic shared-memory limit once per device (the attribute persists per
-// device context; setting it on every launch costs host time for nothing). Templated on the
+// Sets a kernel's dynamic shared-memory limit once per device context (the attribute persists
+// in the context; setting it on every launch costs host time for nothing). Templated on the
 // kernel pointer itself, so every kernel instantiation keeps its own per-device record even when
 // several share one signature.
 template <auto Kernel>
 inline cudaError_t ensure_smem_limit(int bytes) {
-    static unsigned long long done_mask = 0;  // bit d: set on device d (benign race: idempotent)
+    static unsigned long long done_ctx[64] = {};  // context id per device where it is set
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);
     if (err != cudaSuccess) {
         return err;
     }
-    const unsigned long long bit = (dev >= 0 && dev < 64) ? (1ull << dev) : 0ull;
-    if (bit != 0 && (__atomic_load_n(&done_mask, __ATOMIC_ACQUIRE) & bit) != 0) {
+    const bool tracked = dev >= 0 && dev < 64;
+    const unsigned long long ctx = current_context_id();
+    if (tracked && ctx != 0 && __atomic_load_n(&done_ctx[dev], __ATOMIC_ACQUIRE) == ctx) {
         return cudaSuccess;
     }
     err = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    if (err == cudaSuccess && bit != 0) {
-        __atomic_fetch_or(&done_mask, bit, __ATOMIC_RELEASE);
+    if (err == cudaSuccess && tracked) {
+        // The call above made the device's context current if none was.
+        __atomic_store_n(&done_ctx[dev], current_context_id(), __ATOMIC_RELEASE);
     }
     return err;
 }

@@ -26,13 +26,9 @@
 //                       warp 1: MMA issuer (one thread) and TMEM allocation; warp 2: the
 //                       issuer of query tile 1 where tiles have their own issuers (d = 64);
 //                       the remaining warps idle.
-//   Build options (measured on B200, off by default): FA_SPLIT_COLS=2 gives each query tile
-//   two softmax warpgroups that split its 128 key columns and exchange row maxima and sums
-//   through shared memory over a 64-thread named barrier; FA_REGS_SOFTMAX=R (184 at d = 128
-//   by default) moves registers from the producer/MMA warpgroup to the softmax warpgroups
-//   (setmaxnreg); FA_PERSISTENT=1 uses the persistent grid at every N; FA_PING_PONG=1
-//   makes the two tiles' softmax warps of each sub-partition take turns at the exponentials
-//   (d = 64); FA_ISSUER_SMSP_SWAP=1 moves the two d = 64 issuers to sub-partitions 0 and 3.
+//   Tuning knobs (compile-time, defaults measured fastest on B200): the software-2^x share and
+//   polynomial degree, the MMA issuer count, the d = 64 ring depth and the register split
+//   between the softmax warpgroups and the producer/MMA warpgroup (setmaxnreg).
 //
 // Tensor memory (512 columns x 128 lanes, fp32 cells):
 //   S_t  columns [128 t, 128 t + 128)   scores of tile t, fp32
@@ -70,9 +66,6 @@
 #ifndef FA_REGS_SOFTMAX
 #define FA_REGS_SOFTMAX 184  // softmax warps' registers with two query tiles (setmaxnreg; 0 = none)
 #endif
-// Softmax warpgroups per query tile (fp32 variants): 2 splits the 128 columns of S between two
-// warpgroups that own the same rows and exchange row maxima through shared memory. Measured on
-// B200 at d = 128: no faster than 1 (the exponentials, not the warps' latency, bound a tile).
 // Degree of the software 2^x polynomial per head dim (3 = the reference's cubic, 4 = ours).
 #ifndef FA_EXP_POLY_DEG_D128
 #define FA_EXP_POLY_DEG_D128 3
@@ -94,35 +87,11 @@
 #ifndef FA_MMA_ISSUERS_ACC16
 #define FA_MMA_ISSUERS_ACC16 1
 #endif
-#ifndef FA_MIXED_SUM
-#define FA_MIXED_SUM 1  // row sum via add.rn.f32.f16 instead of a conversion and a packed add
-#endif
 #ifndef FA_STAGES_D64
 #define FA_STAGES_D64 8  // K/V ring slots at d = 64 (16 KB each)
 #endif
-#ifndef FA_PERSISTENT_MAX_N
-#define FA_PERSISTENT_MAX_N 2048  // persistent grid for N up to this
-#endif
-#ifndef FA_O_STORE_TMA
-#define FA_O_STORE_TMA 1  // one item per CTA: O through the Q buffer and a TMA store
-#endif
 #ifndef FA_REGS_SOFTMAX_D64
 #define FA_REGS_SOFTMAX_D64 0  // d = 64: no setmaxnreg (measured faster)
-#endif
-#ifndef FA_PERSISTENT
-#define FA_PERSISTENT 0  // 1: every launch on a persistent grid (one CTA per SM walks the items)
-#endif
-#ifndef FA_PING_PONG
-#define FA_PING_PONG 0  // separate P (d = 64): the two tiles take turns at the exponentials
-#endif
-#ifndef FA_ISSUER_SMSP_SWAP
-#define FA_ISSUER_SMSP_SWAP 0
-#endif
-#ifndef FA_LATE_P_WAIT
-#define FA_LATE_P_WAIT 1  // separate P columns (d = 64): wait for the previous P.V at the P store
-#endif
-#ifndef FA_SPLIT_COLS
-#define FA_SPLIT_COLS 1
 #endif
 
 namespace fa_sm100 {
@@ -130,6 +99,7 @@ namespace fa_sm100 {
 constexpr int kBM = 128;             // query rows per tile (= TMEM lanes = MMA M)
 constexpr int kBN = 128;             // keys per K/V tile (= MMA N of Q K^T)
 constexpr int kBoxBytes = 128 * 128; // one TMA box: 128 rows x 64 fp16 (128 B, one swizzle span)
+constexpr int kPersistentMaxN = 2048; // persistent grid (one CTA per SM walks the items) up to this N
 
 template <int D_, bool CAUSAL_, int VARIANT_>
 struct FwdCfg {
@@ -171,20 +141,15 @@ struct FwdCfg {
     static constexpr int tmem_t1(int t) { return T_HI_IN_S ? (kTmemS + kBN * t + 64) : (kTmemExtra + D); }
     static constexpr int kTmemCols = 512;
     static_assert(kTmemUsed <= kTmemCols, "tensor memory budget");
-    // Warps: NQ x SPLIT softmax warpgroups + one producer/MMA warpgroup. With SPLIT = 2 the
-    // warpgroup (t, h) owns rows 0..127 of query tile t and S columns [64 h, 64 h + 64).
-    static constexpr int SPLIT = ACC16 ? 1 : FA_SPLIT_COLS;
-    static constexpr int kCols = kBN / SPLIT;  // S columns per softmax thread
-    static constexpr int kSoftmaxWarps = 4 * NQ * SPLIT;
+    // Warps: NQ softmax warpgroups + one producer/MMA warpgroup.
+    static constexpr int kSoftmaxWarps = 4 * NQ;
     static constexpr int kIssuers =  // MMA issuer warps kMmaWarp and kIssuerWarp1
         (NQ == 2 && (ACC16 ? FA_MMA_ISSUERS_ACC16 : (D == 64 ? FA_MMA_ISSUERS_D64 : FA_MMA_ISSUERS_D128)) == 2)
             ? 2
             : 1;
-    // FA_ISSUER_SMSP_SWAP (two issuers): issuers on warps 8 + 0 and 8 + 3, producer on 8 + 1.
-    static constexpr bool kSwap = FA_ISSUER_SMSP_SWAP && kIssuers == 2;
-    static constexpr int kProducerWarp = kSoftmaxWarps + (kSwap ? 1 : 0);
-    static constexpr int kMmaWarp = kSoftmaxWarps + (kSwap ? 0 : 1);
-    static constexpr int kIssuerWarp1 = kSwap ? kSoftmaxWarps + 3 : kMmaWarp + 1;
+    static constexpr int kProducerWarp = kSoftmaxWarps;
+    static constexpr int kMmaWarp = kSoftmaxWarps + 1;
+    static constexpr int kIssuerWarp1 = kMmaWarp + 1;
     static constexpr int kThreads = 32 * (kSoftmaxWarps + 4);
     // Register split: every warp is launched with kRegsLaunch (65536 / threads, a multiple of
     // 8); with FA_REGS_SOFTMAX != 0 the softmax warpgroups go to that many and the
@@ -201,17 +166,9 @@ struct FwdCfg {
                       (32 * kSoftmaxWarps * kRegsSoftmax + 128 * kRegsOther <= kThreads * kRegsLaunch &&
                        kRegsOther >= 24 && kRegsSoftmax % 8 == 0 && kRegsSoftmax <= 256),
                   "register split exceeds the launch allocation");
-    static_assert(SPLIT == 1 || SPLIT == 2, "column split");
     static_assert(D == 64 || D == 128, "head dim");
     static_assert(kSmemAlloc <= 227 * 1024, "shared memory budget");
     static_assert(kSmemAlloc > 114 * 1024, "one CTA per SM (it owns all 512 TMEM columns)");
-};
-
-// Row statistics exchanged between the two column halves of a query tile (SPLIT = 2):
-// red_max[j % 2][t][h][row] per key tile, red_sum[t][h][row] once at the end.
-struct SharedRowStats {
-    float red_max[2][2][2][128];
-    float red_sum[2][2][128];
 };
 
 constexpr int kMaxStages = 16;
@@ -229,59 +186,6 @@ struct SharedBarriers {
     uint32_t tmem_base;
     int abort;
 };
-
-// Optional event trace of one CTA (build with -DFA_TRACE; off in the product build): SM clock
-// stamps of the pipeline events of CTA (gridDim.x / 2, 0), read back with fa_trace_read().
-#ifdef FA_TRACE
-// [0, 2*4*64): softmax t (key tile j < 64): {S ready, S loaded, P stored + arrived, row max}
-// [1024, +2*4*64): MMA t: {P ready, PV issued, S(j+1) issued, V ready}
-// [2048, +256): producer ring slot: load issued
-// [2304, +2*4*64): softmax t, key tile j: arrival on P-ready of each of the tile's four warps
-// [3328, +2*4*64): issuer t (d = 64), key tile j: {S_t(j) free, K(j+1) landed}
-// [3840, +2*4*64): softmax t, key tile j: S loaded, per warp of the tile
-// [4352, +2*4*64): ... row max done, per warp; [4864, +2*4*64): ... late P wait done, per warp
-// [2816, +2*4*64): softmax t, key tile j: {fp16acc: fold of the fp16 partials done, wait for the
-//                  previous P.V (before a rescale or a separate-P store) done}
-__device__ unsigned long long g_fa_trace[8192];
-// Per CTA (linear id < 16384): {SM clock at entry, SM clock at exit, global timer at entry,
-// global timer at exit, SM id}.
-constexpr int kCtaTraceMax = 16384;
-__device__ unsigned long long g_fa_cta_trace[kCtaTraceMax * 5];
-__device__ __forceinline__ unsigned long long global_timer_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-__device__ __forceinline__ void trace_cta_time(int slot) {
-    const unsigned lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
-    if (threadIdx.x == 0 && lin < kCtaTraceMax) {
-        g_fa_cta_trace[lin * 5 + slot] = clock64();
-        g_fa_cta_trace[lin * 5 + 2 + slot] = global_timer_ns();
-        if (slot == 0) {
-            unsigned sm;
-            asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
-            g_fa_cta_trace[lin * 5 + 4] = sm;
-        }
-    }
-}
-#define FA_TRACE_CTA(slot) trace_cta_time(slot)
-__device__ __forceinline__ bool trace_cta() {
-    return blockIdx.x == gridDim.x / 2 && blockIdx.y == 0;
-}
-#define FA_TRACE_AT(idx)                                      \
-    do {                                                      \
-        if (trace_cta()) {                                    \
-            g_fa_trace[(idx)] = clock64();                    \
-        }                                                     \
-    } while (0)
-#else
-#define FA_TRACE_AT(idx) \
-    do {                 \
-    } while (0)
-#define FA_TRACE_CTA(slot) \
-    do {                   \
-    } while (0)
-#endif
 
 // fp16 accumulator cells hold one value per 32-bit column, in the low half.
 __device__ __forceinline__ float f16cell_to_float(uint32_t cell) {
@@ -343,9 +247,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 
     extern __shared__ uint8_t smem_raw[];
     __shared__ SharedBarriers sb;
-    __shared__ SharedRowStats rs;
 
-    FA_TRACE_CTA(0);
     const int warp = static_cast<int>(threadIdx.x) / 32;
     const int lane = static_cast<int>(threadIdx.x) % 32;
 
@@ -420,7 +322,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     // O leaves through the Q buffer and a TMA store when each CTA runs one item (the buffer is
     // free once the item's last S MMA has completed); a persistent CTA reloads Q for its next
     // item meanwhile, so there each thread stores its row directly.
-    const bool tma_store_o = FA_O_STORE_TMA && grid_n >= args.num_items;
+    const bool tma_store_o = grid_n >= args.num_items;
 
     if (threadIdx.x == 0) {
         sb.abort = 0;
@@ -430,10 +332,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             mbar_init(smem_u32(&sb.s_full[t]), 1);
             // Softmax-side barriers take one arrival per warp (after __syncwarp), not one per
             // thread: 128 arrivals on one barrier word serialise in the shared-memory atomics.
-            mbar_init(smem_u32(&sb.s_free[t]), 4 * Cfg::SPLIT);
-            mbar_init(smem_u32(&sb.p_full[t]), 4 * Cfg::SPLIT);
+            mbar_init(smem_u32(&sb.s_free[t]), 4);
+            mbar_init(smem_u32(&sb.p_full[t]), 4);
             mbar_init(smem_u32(&sb.o_done[t]), 1);
-            mbar_init(smem_u32(&sb.epi[t]), 4 * Cfg::SPLIT);
+            mbar_init(smem_u32(&sb.epi[t]), 4);
         }
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(smem_u32(&sb.kv_full[s]), 1);
@@ -471,19 +373,14 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     // of its tile, so the waits take their parity from running counts kept by each role.
     if (warp < Cfg::kSoftmaxWarps) {
         // ================================ softmax warpgroups ================================
-        constexpr int SPLIT = Cfg::SPLIT;
-        constexpr int NC = Cfg::kCols;                 // S columns of this thread
-        const int t = (warp / 4) % NQ;                  // query tile
-        const int half = warp / (4 * NQ);               // column half (0 when SPLIT == 1)
+        constexpr int NC = kBN;                         // S columns of this thread
+        const int t = warp / 4;                         // query tile
         const int row = (warp % 4) * 32 + lane;         // TMEM lane == query row within the tile
-        const int col0 = half * NC;                     // first S column of this thread
-        const int pair_id = 1 + t * 4 + (warp % 4);     // named barrier of the two halves
         const uint32_t lane_off = static_cast<uint32_t>((warp % 4) * 32) << 16;
-        const uint32_t t_s = tmem + lane_off + Cfg::kTmemS + t * kBN + col0;
-        constexpr int OC = D / SPLIT;                   // O columns this thread rescales / stores
-        const uint32_t t_o = tmem + lane_off + Cfg::kTmemO + t * D + half * OC;
-        const uint32_t t_p = (Cfg::SEP_P ? (tmem + lane_off + Cfg::kTmemExtra + t * 64)
-                                         : (tmem + lane_off + Cfg::kTmemS + t * kBN)) + col0 / 2;
+        const uint32_t t_s = tmem + lane_off + Cfg::kTmemS + t * kBN;
+        const uint32_t t_o = tmem + lane_off + Cfg::kTmemO + t * D;
+        const uint32_t t_p = Cfg::SEP_P ? (tmem + lane_off + Cfg::kTmemExtra + t * 64)
+                                        : (tmem + lane_off + Cfg::kTmemS + t * kBN);
         const uint32_t t_t0 = tmem + lane_off + Cfg::tmem_t0(t);
         const uint32_t t_t1 = tmem + lane_off + Cfg::tmem_t1(t);
         const uint32_t bar_s = smem_u32(&sb.s_full[t]);
@@ -491,19 +388,15 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         const uint32_t bar_p = smem_u32(&sb.p_full[t]);
         const uint32_t bar_o = smem_u32(&sb.o_done[t]);
         const float scale_log2 = args.scale_log2;
-        const int pp_mine = 1 + (warp % 4) * 2 + t;
-        const int pp_other = 1 + (warp % 4) * 2 + (t ^ 1);
-        constexpr bool kPingPong = Cfg::SEP_P && SPLIT == 1 && NQ == 2 && FA_PING_PONG;
         // With P in its own columns the wait for the previous P.V is deferred to the first P
         // store, so the exponentials of the first chunk overlap that P.V.
-        constexpr bool kLateWait = Cfg::SEP_P && FA_LATE_P_WAIT;
+        constexpr bool kLateWait = Cfg::SEP_P;
 
         int g0 = 0;  // S / P / P.V count of this tile before the current item
         bool ok = true;
 
         // A warp that gave up on a wait keeps walking its items and key tiles without touching
-        // TMEM, so that the two column halves of a row always pass the same number of pair
-        // barriers (and the two tiles the same number of ping-pong barriers).
+        // TMEM (every later wait returns at once), so that all roles leave their loops.
         for (int r = 0;; ++r) {
             const int idx = item_index(r);
             if (idx < 0) {
@@ -511,16 +404,14 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             }
             // Only what the key-tile loop needs stays live through it; the epilogue decodes the
             // item again for its head and key range.
-            int q0, nt, kv0, pp_turns;
+            int q0, nt, kv0;
             {
                 Item it;
                 decode(idx, it);
                 q0 = it.q_row0 + t * kBM;
                 nt = (t == 0) ? it.n_kv[0] : it.n_kv[NQ - 1];  // a select keeps `it` in registers
                 kv0 = it.kv0;
-                pp_turns = kPingPong ? min(it.n_kv[0], it.n_kv[NQ - 1]) : 0;
             }
-            [[maybe_unused]] const bool fa_tr = (r == 0);  // trace builds: first item only
             const int grow = q0 + row;  // global query row
             // Last key index this row may see: keys > lim are masked (ragged N, causal).
             const int lim = Cfg::CAUSAL ? min(n - 1, grow) : (n - 1);
@@ -528,40 +419,11 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             float row_max = -INFINITY;  // running max of the scaled scores (log2 units)
             float row_sum = 0.0f;       // running sum of this thread's fp16-rounded probabilities
 
-            // Exponential ping-pong (FA_PING_PONG, separate P): the two query tiles' warps on one
-            // SM sub-partition (warps q and q + 4) take turns at the exponential loop. Warp q of
-            // tile t waits on barrier pp_mine and releases the other tile's; tile 0 goes first
-            // (tile 1 releases it once per item). Both tiles take turns for the first
-            // min(n_kv[0], n_kv[1]) key tiles of the item only, and every path through an
-            // iteration passes the same barriers, so arrivals and waits always pair up.
-            auto pp_enter = [&](int j) {
-                if (kPingPong && j < pp_turns) {
-                    named_bar_sync(pp_mine, 64);
-                }
-            };
-            auto pp_leave = [&](int j) {
-                if (kPingPong && j < pp_turns && !(t == 1 && j == pp_turns - 1)) {
-                    named_bar_arrive(pp_other, 64);
-                }
-            };
-            if (kPingPong && t == 1 && pp_turns > 0) {
-                named_bar_arrive(pp_other, 64);
-            }
-
             for (int j = 0; j < nt; ++j) {
                 const int gj = g0 + j;  // running index of S_t(j), P_t(j) and P.V_t(j)
-                const bool tr = fa_tr && j < 64;
                 ok = ok && __all_sync(0xffffffffu, mbar_wait(bar_s, gj & 1, wctx, kStatusTimeoutSoftmax));
                 if (!ok) {
-                    if constexpr (SPLIT == 2) {
-                        pair_sync(pair_id);
-                    }
-                    pp_enter(j);
-                    pp_leave(j);
                     continue;
-                }
-                if (row == 0 && half == 0 && tr) {
-                    FA_TRACE_AT((t * 64 + j) * 4 + 0);
                 }
                 tc_fence_after();
                 uint32_t sr[NC];
@@ -570,12 +432,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     tmem_ld32(t_s + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
                 }
                 tmem_wait_ld();
-                if (row == 0 && half == 0 && tr) {
-                    FA_TRACE_AT((t * 64 + j) * 4 + 1);
-                }
-                if (lane == 0 && half == 0 && tr) {
-                    FA_TRACE_AT(3840 + (t * 64 + j) * 4 + (warp % 4));
-                }
                 if constexpr (Cfg::SEP_P) {
                     // S_t is in registers: the MMA warp may overwrite it with the next S_t.
                     tc_fence_before();
@@ -594,7 +450,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 float mul;
                 if (masked) {
                     // Scale first, then mask, so masked scores are -inf whatever the scale's sign.
-                    const int cmax = lim - kbase - col0;
+                    const int cmax = lim - kbase;
 #pragma unroll
                     for (int c = 0; c < NC; ++c) {
                         sr[c] = f2u((c > cmax) ? -INFINITY : u2f(sr[c]) * scale_log2);
@@ -607,23 +463,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                                                    : row_extreme<false, NC>(sr)) *
                                scale_log2;
                     mul = scale_log2;
-                }
-                if constexpr (SPLIT == 2) {
-                    // Row max over both column halves (one buffer per key-tile parity, so a half
-                    // that runs ahead never overwrites a value its partner has yet to read). A
-                    // partner that aborted meets this barrier from its own branch above; the
-                    // value read is then stale, and the abort flag stops this warp at its next
-                    // wait.
-                    rs.red_max[gj & 1][t][half][row] = tile_max;
-                    pair_sync(pair_id);
-                    tile_max = fmaxf(tile_max, rs.red_max[gj & 1][t][half ^ 1][row]);
-                }
-
-                if (row == 0 && half == 0 && tr) {
-                    FA_TRACE_AT((t * 64 + j) * 4 + 3);
-                }
-                if (lane == 0 && half == 0 && tr) {
-                    FA_TRACE_AT(4352 + (t * 64 + j) * 4 + (warp % 4));
                 }
                 // Running max update (lazy for "opt": keep the old max unless it grew by > 2^8).
                 const float new_max = (tile_max > row_max + Cfg::kRescaleThreshold) ? tile_max : row_max;
@@ -639,14 +478,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     ok = __all_sync(0xffffffffu,
                                     mbar_wait(bar_o, (gj - 1) & 1, wctx, kStatusTimeoutSoftmax));
                     if (!ok) {
-                        pp_enter(j);
-                        pp_leave(j);
                         continue;
                     }
                     tc_fence_after();
-                    if (row == 0 && half == 0 && tr) {
-                        FA_TRACE_AT(2816 + (t * 64 + j) * 4 + 1);
-                    }
                 }
 
                 // Probabilities, packed fp16 pairs, into P_t.
@@ -657,7 +491,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 for (int i = 0; i < 4; ++i) {
                     sum2[i] = make_float2(0.0f, 0.0f);
                 }
-                pp_enter(j);
 #pragma unroll
                 for (int chunk = 0; chunk < NC / 64; ++chunk) {
                     uint32_t pk[32];
@@ -678,12 +511,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                         // is normalised by the weights it was accumulated with. (The reference
                         // sums the fp32 values, csrc/kernels/flash_fwd.cu:403-417; measured here
                         // that adds error: cfg4's outlier rows exceed 2e-3.)
-#if FA_MIXED_SUM
                         // fp32 += fp16 with the mixed-precision add (no separate conversion).
                         add_f16x2_to_f32(sum2[i % 4].x, sum2[i % 4].y, h);
-#else
-                        sum2[i % 4] = __fadd2_rn(sum2[i % 4], unpack_half2(h));
-#endif
                         pk[i] = h;
                     }
                     if (kLateWait && chunk == 0 && j > 0) {
@@ -692,19 +521,12 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                                         mbar_wait(bar_o, (gj - 1) & 1, wctx, kStatusTimeoutSoftmax));
                         if (ok) {
                             tc_fence_after();
-                            if (row == 0 && half == 0 && tr) {
-                                FA_TRACE_AT(2816 + (t * 64 + j) * 4 + 1);
-                            }
-                            if (lane == 0 && half == 0 && tr) {
-                                FA_TRACE_AT(4864 + (t * 64 + j) * 4 + (warp % 4));
-                            }
                         }
                     }
                     if (ok) {
                         tmem_st32(t_p + chunk * 32, pk);
                     }
                 }
-                pp_leave(j);
                 if (!ok) {
                     continue;
                 }
@@ -717,7 +539,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     if (need_rescale) {
                         const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll
-                        for (int c = 0; c < OC / 32; ++c) {
+                        for (int c = 0; c < D / 32; ++c) {
                             uint32_t o[32];
                             tmem_ld32(t_o + c * 32, o);
                             tmem_wait_ld();
@@ -735,12 +557,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     __syncwarp();
                     if (lane == 0) {
                         mbar_arrive(bar_p);
-                        if (half == 0 && tr) {
-                            FA_TRACE_AT(2304 + (t * 64 + j) * 4 + (warp % 4));
-                        }
-                    }
-                    if (row == 0 && half == 0 && tr) {
-                        FA_TRACE_AT((t * 64 + j) * 4 + 2);
                     }
                 } else {
                     tmem_wait_st();
@@ -748,9 +564,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     __syncwarp();
                     if (lane == 0) {
                         mbar_arrive(bar_p);
-                    }
-                    if (row == 0 && tr) {
-                        FA_TRACE_AT((t * 64 + j) * 4 + 2);
                     }
                     // Fold this tile's two fp16 partials into the fp32 accumulator:
                     // O = alpha * O + T_0 + T_1.
@@ -787,9 +600,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                             mbar_arrive(bar_sf);
                         }
                     }
-                    if (row == 0 && tr) {
-                        FA_TRACE_AT(2816 + (t * 64 + j) * 4);
-                    }
                 }
             }
 
@@ -803,14 +613,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     tc_fence_after();
                 }
             }
-            if constexpr (SPLIT == 2) {
-                // Row sum over both column halves. Both warps of the pair reach this barrier:
-                // they share every loop decision above (same waits, votes and maxima), so either
-                // both are here with ok, or both aborted at the same step.
-                rs.red_sum[t][half][row] = row_sum;
-                pair_sync(pair_id);
-                row_sum += rs.red_sum[t][half ^ 1][row];
-            }
             Item it;
             decode(idx, it);
             if (split) {
@@ -821,10 +623,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 if (q0 < n && (ok || nt == 0)) {
                     const size_t rec =
                         (static_cast<size_t>(it.z) * args.num_bh + it.bh) * args.rows_pad + grow;
-                    float4* dst = reinterpret_cast<float4*>(args.ws_o + rec * D + half * OC);
+                    float4* dst = reinterpret_cast<float4*>(args.ws_o + rec * D);
                     if (nt > 0) {
 #pragma unroll
-                        for (int c = 0; c < OC / 32; ++c) {
+                        for (int c = 0; c < D / 32; ++c) {
                             uint32_t o[32];
                             tmem_ld32(t_o + c * 32, o);
                             tmem_wait_ld();
@@ -836,14 +638,12 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                         }
                     } else {
 #pragma unroll
-                        for (int i = 0; i < OC / 4; ++i) {
+                        for (int i = 0; i < D / 4; ++i) {
                             dst[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                         }
                     }
-                    if (half == 0) {
-                        reinterpret_cast<float2*>(args.ws_ml)[rec] =
-                            make_float2(nt > 0 ? row_max : -INFINITY, nt > 0 ? row_sum : 0.0f);
-                    }
+                    reinterpret_cast<float2*>(args.ws_ml)[rec] =
+                        make_float2(nt > 0 ? row_max : -INFINITY, nt > 0 ? row_sum : 0.0f);
                 }
             } else if (tma_store_o && ok && nt > 0) {
                 const float inv_sum = (row_sum > 0.0f) ? (1.0f / row_sum) : 0.0f;
@@ -851,7 +651,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 // Every MMA that read Q_t has completed (its S was consumed above).
                 uint8_t* out = smem + Cfg::kSmemQ + t * Cfg::kTileBytes;
 #pragma unroll
-                for (int c = 0; c < OC / 32; ++c) {
+                for (int c = 0; c < D / 32; ++c) {
                     uint32_t o[32];
                     tmem_ld32(t_o + c * 32, o);
                     tmem_wait_ld();
@@ -860,7 +660,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     for (int e = 0; e < 16; ++e) {
                         h[e] = pack_half2(u2f(o[2 * e]) * inv_sum, u2f(o[2 * e + 1]) * inv_sum);
                     }
-                    const int col = half * OC + c * 32;  // first O column of this chunk
+                    const int col = c * 32;  // first O column of this chunk
                     const int box = col / 64;
                     const int chunk0 = (col % 64) / 8;
 #pragma unroll
@@ -876,7 +676,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 if (lane == 0) {
                     mbar_arrive(smem_u32(&sb.epi[t]));
                 }
-                if (row == 0 && half == 0) {
+                if (row == 0) {
                     if (mbar_wait(smem_u32(&sb.epi[t]), 0, wctx, kStatusTimeoutEpilogue)) {
 #pragma unroll
                         for (int b = 0; b < Cfg::kBoxes; ++b) {
@@ -888,13 +688,13 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 }
                 __syncwarp();
             } else if (ok && nt > 0) {
-                // O row (this thread's OC columns), normalised, as fp16 straight to global
+                // O row (this thread's D columns), normalised, as fp16 straight to global
                 // memory: 16-byte stores, rows >= N skipped.
                 const float inv_sum = (row_sum > 0.0f) ? (1.0f / row_sum) : 0.0f;
                 uint4* dst = reinterpret_cast<uint4*>(args.o) +
-                             ((static_cast<size_t>(it.bh) * n + grow) * D + half * OC) / 8;
+                             ((static_cast<size_t>(it.bh) * n + grow) * D) / 8;
 #pragma unroll
-                for (int c = 0; c < OC / 32; ++c) {
+                for (int c = 0; c < D / 32; ++c) {
                     uint32_t o[32];
                     tmem_ld32(t_o + c * 32, o);
                     tmem_wait_ld();
@@ -937,7 +737,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 }
                 Item it;
                 decode(idx, it);
-                [[maybe_unused]] const bool fa_tr = (r == 0);
 #pragma unroll
                 for (int t = 0; t < NQ; ++t) {
                     if (ok && it.n_kv[t] > 0) {
@@ -978,9 +777,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                         }
                         loaded[stage] = true;
                         last_parity[stage] = phase;
-                        if (fa_tr && ring < 256) {
-                            FA_TRACE_AT(2048 + ring);
-                        }
                         ++ring;
                     }
                 }
@@ -1032,7 +828,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 }
                 Item it;
                 decode(idx, it);
-                [[maybe_unused]] const bool fa_tr = (r == 0);
                 const int n_t = (t == 0) ? it.n_kv[0] : it.n_kv[NQ - 1];
                 const int n_max = it.n_max;
                 if (n_t > 0) {
@@ -1067,7 +862,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     }
                 }
                 for (int j = 0; ok && j < n_max; ++j) {
-                    const bool tr = fa_tr && j < 64;
                     const int v_slot = ring++;
                     const int vs = v_slot % STAGES;
                     const bool has_next = (j + 1 < n_max);
@@ -1081,16 +875,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                             // S_t(j+1) as soon as the softmax has S_t(j) in registers.
                             if (next_s) {
                                 ok = mbar_wait(smem_u32(&sb.s_free[t]), (s_cnt - 1) & 1, wctx, kStatusTimeoutMma);
-                                if (tr) {
-                                    FA_TRACE_AT(3328 + (t * 64 + j) * 4 + 0);
-                                }
                                 ok = ok && mbar_wait(smem_u32(&sb.kv_full[ks]), (k_slot / STAGES) & 1, wctx,
                                                      kStatusTimeoutMma);
                                 if (!ok) {
                                     break;
-                                }
-                                if (tr) {
-                                    FA_TRACE_AT(3328 + (t * 64 + j) * 4 + 1);
                                 }
                                 k_ready = true;
                                 tc_fence_after();
@@ -1100,15 +888,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                                     umma_commit(smem_u32(&sb.q_empty[t]));
                                 }
                                 ++s_cnt;
-                                if (tr) {
-                                    FA_TRACE_AT(1024 + (t * 64 + j) * 4 + 2);
-                                }
                             }
                         }
                         ok = mbar_wait(smem_u32(&sb.p_full[t]), pv_cnt & 1, wctx, kStatusTimeoutMma);
-                        if (tr) {
-                            FA_TRACE_AT(1024 + (t * 64 + j) * 4 + 0);
-                        }
                         ok = ok && mbar_wait(smem_u32(&sb.kv_full[vs]), (v_slot / STAGES) & 1, wctx,
                                              kStatusTimeoutMma);
                         if (!ok) {
@@ -1123,9 +905,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                         }
                         umma_commit(smem_u32(&sb.o_done[t]));
                         ++pv_cnt;
-                        if (tr) {
-                            FA_TRACE_AT(1024 + (t * 64 + j) * 4 + 1);
-                        }
                         if constexpr (!Cfg::SEP_P) {
                             // S_t(j+1) reuses the columns P_t(j) was read from by the MMAs above
                             // (tcgen05.mma operations of one thread execute in issue order); with
@@ -1148,9 +927,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                                     umma_commit(smem_u32(&sb.q_empty[t]));
                                 }
                                 ++s_cnt;
-                                if (tr) {
-                                    FA_TRACE_AT(1024 + (t * 64 + j) * 4 + 2);
-                                }
                             }
                         }
                     } else {
@@ -1224,7 +1000,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 }
                 Item it;
                 decode(idx, it);
-                [[maybe_unused]] const bool fa_tr = (r == 0);
                 const int n_max = it.n_max;
 #pragma unroll
                 for (int t = 0; t < NQ; ++t) {
@@ -1250,7 +1025,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     }
                 }
                 for (int j = 0; ok && j < n_max; ++j) {
-                    const bool tr = fa_tr && j < 64;
                     const int v_slot = ring++;
                     const int vs = v_slot % STAGES;
                     const bool has_next = (j + 1 < n_max);
@@ -1280,9 +1054,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                             }
                         }
                         ok = mbar_wait(smem_u32(&sb.p_full[t]), pv_cnt[t] & 1, wctx, kStatusTimeoutMma);
-                        if (tr) {
-                            FA_TRACE_AT(1024 + (t * 64 + j) * 4 + 0);
-                        }
                         if (ok && !v_ready) {
                             ok = mbar_wait(smem_u32(&sb.kv_full[vs]), (v_slot / STAGES) & 1, wctx,
                                            kStatusTimeoutMma);
@@ -1303,9 +1074,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                         }
                         umma_commit(smem_u32(&sb.o_done[t]));
                         ++pv_cnt[t];
-                        if (tr) {
-                            FA_TRACE_AT(1024 + (t * 64 + j) * 4 + 1);
-                        }
                         if constexpr (!Cfg::SEP_P) {
                             // S_t(j+1) reuses the columns P_t(j) was read from by the MMAs above;
                             // with fp16acc also those of T_1, once the softmax has folded it.
@@ -1318,9 +1086,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                                 ok = ok && issue_s(t, ks, j + 2 == it.n_kv[t]);
                                 if (!ok) {
                                     break;
-                                }
-                                if (tr) {
-                                    FA_TRACE_AT(1024 + (t * 64 + j) * 4 + 2);
                                 }
                             }
                         }
@@ -1347,7 +1112,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem, Cfg::kTmemCols);
     }
-    FA_TRACE_CTA(1);
 }
 
 // Split-KV combine (reference: none; Flash-Decoding's merge of per-range softmax partials).
@@ -1447,7 +1211,7 @@ cudaError_t launch_cfg(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const C
     const double kv_bytes = 4.0 * static_cast<double>(args.seqlen) * D;
     launch_args.head_group =
         static_cast<int>(std::min<double>(args.num_bh, std::max(1.0, (48.0 * 1048576.0) / kv_bytes)));
-    // One work item per (row block, head, key range). Short rows (N <= FA_PERSISTENT_MAX_N) run
+    // One work item per (row block, head, key range). Short rows (N <= kPersistentMaxN) run
     // on a persistent grid of one CTA per SM that walks the items, so that each item's Q load
     // and first S overlap the previous item's tail (measured: B16 H16 N1000 d128 causal 496 ->
     // 554 TFLOPS); longer rows run one CTA per item (cfg1 N4096: 911 vs 862 persistent).
@@ -1457,7 +1221,7 @@ cudaError_t launch_cfg(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const C
         return cudaErrorInvalidValue;
     }
     launch_args.num_items = static_cast<int>(items);
-    const bool persistent = FA_PERSISTENT || (args.seqlen <= FA_PERSISTENT_MAX_N);
+    const bool persistent = args.seqlen <= kPersistentMaxN;
     const long long ctas = persistent ? std::min<long long>(items, device_sm_count()) : items;
     kernel<<<dim3(static_cast<unsigned>(ctas)), Cfg::kThreads, Cfg::kSmemAlloc, stream>>>(tm_q, tm_k, tm_v,
                                                                                          tm_o, launch_args);
@@ -1560,40 +1324,6 @@ int kernel_rows_per_cta(int head_dim, int variant) {
                                           : FwdCfg<128, false, kVariantOpt>::NQ));
 }
 
-#ifdef FA_TRACE
-int trace_read(unsigned long long* out, int n) {
-    if (n > 8192) {
-        n = 8192;
-    }
-    return cudaMemcpyFromSymbol(out, g_fa_trace, sizeof(unsigned long long) * n) == cudaSuccess ? n : -1;
-}
-int trace_clear() {
-    static unsigned long long zero[kCtaTraceMax * 5] = {};
-    if (cudaMemcpyToSymbol(g_fa_cta_trace, zero, sizeof(zero)) != cudaSuccess) {
-        return -1;
-    }
-    return cudaMemcpyToSymbol(g_fa_trace, zero, sizeof(unsigned long long) * 8192) == cudaSuccess ? 0 : -1;
-}
-int trace_cta_read(unsigned long long* out, int n_cta) {
-    if (n_cta > kCtaTraceMax) {
-        n_cta = kCtaTraceMax;
-    }
-    return cudaMemcpyFromSymbol(out, g_fa_cta_trace, sizeof(unsigned long long) * 5 * n_cta) == cudaSuccess
-               ? n_cta
-               : -1;
-}
-#endif
 
 }  // namespace fa_sm100
 
-#ifdef FA_TRACE
-extern "C" __attribute__((visibility("default"))) int fa_trace_read(unsigned long long* out, int n) {
-    return fa_sm100::trace_read(out, n);
-}
-extern "C" __attribute__((visibility("default"))) int fa_trace_clear(void) {
-    return fa_sm100::trace_clear();
-}
-extern "C" __attribute__((visibility("default"))) int fa_trace_cta_read(unsigned long long* out, int n_cta) {
-    return fa_sm100::trace_cta_read(out, n_cta);
-}
-#endif

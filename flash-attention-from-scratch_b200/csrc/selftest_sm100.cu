@@ -221,194 +221,12 @@ __global__ void watchdog_probe_kernel(int* flags) {
     }
 }
 
-// CTA-pair probe (cluster of 2, cta_group::2): S = Q K^T for 256 query rows (128 per CTA) and
-// 128 keys, with K split between the CTAs (keys 0..63 in the leader, 64..127 in the other), then
-// O = P V with P in each CTA's TMEM and V split by columns (0..63 / 64..127). Loads from both
-// CTAs count on the leader's barrier; the leader issues the pair MMAs and commits to both CTAs'
-// barriers. flags[2r] = 1 if CTA r's waits succeeded, flags[2r+1] = 1 at CTA r's end.
-struct PairShared {
-    uint64_t load_bar;
-    uint64_t s_bar;
-    uint64_t o_bar;
-    uint32_t tmem_base;
-    int abort;
-};
-
-constexpr int kPairQ = 128 * 128 * 2;  // this CTA's 128 Q rows
-constexpr int kPairK = 64 * 128 * 2;   // this CTA's 64 keys of K
-constexpr int kPairV = 128 * 64 * 2;   // this CTA's 64 columns of V
-
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(128, 1)
-    umma_pair_probe_kernel(const __grid_constant__ CUtensorMap tm_q,
-                           const __grid_constant__ CUtensorMap tm_k,
-                           const __grid_constant__ CUtensorMap tm_v, const __half* __restrict__ p,
-                           float* __restrict__ s_out, float* __restrict__ o_out,
-                           int* __restrict__ flags) {
-    extern __shared__ uint8_t smem_raw[];
-    __shared__ PairShared sh;
-    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    const uint32_t base = smem_u32(smem);
-    const uint32_t sq = base;
-    const uint32_t sk = base + kPairQ;
-    const uint32_t sv = sk + kPairK;
-    const int warp = threadIdx.x / 32;
-    const int row = threadIdx.x;
-    const uint32_t rank = cluster_ctarank();
-    const WaitCtx w{&sh.abort, &g_probe_status.code, &g_probe_status.epoch_aborted, 3u};
-
-    if (threadIdx.x == 0) {
-        sh.abort = 0;
-        mbar_init(smem_u32(&sh.load_bar), 1);
-        mbar_init(smem_u32(&sh.s_bar), 1);
-        mbar_init(smem_u32(&sh.o_bar), 1);
-        mbar_fence_init_cluster();
-    }
-    if (warp == 0) {
-        tmem_alloc_pair(smem_u32(&sh.tmem_base), 512);
-        tmem_relinquish_pair();
-    }
-    tc_fence_before();
-    cluster_sync();
-    tc_fence_after();
-    const uint32_t tmem = sh.tmem_base;
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-
-    if (threadIdx.x == 0) {
-        if (rank == 0) {
-            mbar_arrive_expect_tx(smem_u32(&sh.load_bar), 2 * (kPairQ + kPairK + kPairV));
-        }
-        for (int b = 0; b < 2; ++b) {
-            tma_load_3d_pair(sq + b * (kPairQ / 2), &tm_q, smem_u32(&sh.load_bar), b * 64,
-                             static_cast<int>(rank) * 128, 0);
-            tma_load_3d_pair(sk + b * (kPairK / 2), &tm_k, smem_u32(&sh.load_bar), b * 64,
-                             static_cast<int>(rank) * 64, 0);
-        }
-        tma_load_3d_pair(sv, &tm_v, smem_u32(&sh.load_bar), static_cast<int>(rank) * 64, 0, 0);
-    }
-    {
-        // P row (this CTA's row `row`) -> TMEM columns [384, 448), fp16 packed two per column.
-        uint32_t pk[32];
-        const uint32_t* prow = reinterpret_cast<const uint32_t*>(p + (rank * 128 + row) * 128);
-        for (int h = 0; h < 2; ++h) {
-            for (int i = 0; i < 32; ++i) {
-                pk[i] = prow[h * 32 + i];
-            }
-            tmem_st32(tmem + lane_off + 384 + h * 32, pk);
-        }
-        tmem_wait_st();
-    }
-    tc_fence_before();
-    cluster_sync();
-    tc_fence_after();
-
-    if (rank == 0 && threadIdx.x == 0) {
-        bool ok = false;
-        const long long t0 = clock64();
-        while (!(ok = mbar_try_wait_cluster(smem_u32(&sh.load_bar), 0))) {
-            if (clock64() - t0 > (1ll << 31)) {
-                break;
-            }
-        }
-        if (ok) {
-            tc_fence_after();
-            constexpr uint32_t idesc_s = make_idesc_f16(256, 128, true, false);
-            for (int kk = 0; kk < 8; ++kk) {
-                const uint32_t offq = (kk / 4) * (kPairQ / 2) + (kk % 4) * 32;
-                const uint32_t offk = (kk / 4) * (kPairK / 2) + (kk % 4) * 32;
-                umma_ss_pair(tmem + 0, make_desc_kmajor_sw128(sq + offq),
-                             make_desc_kmajor_sw128(sk + offk), idesc_s, kk > 0);
-            }
-            umma_commit_pair(smem_u32(&sh.s_bar));
-            umma_commit_pair(mapa_shared(smem_u32(&sh.s_bar), 1));
-            constexpr uint32_t idesc_o = make_idesc_f16(256, 128, true, true);
-            for (int kk = 0; kk < 8; ++kk) {
-                umma_ts_pair(tmem + 128, tmem + 384 + kk * 8,
-                             make_desc_mnmajor_sw128(sv + kk * 2048, kPairV), idesc_o, kk > 0);
-            }
-            umma_commit_pair(smem_u32(&sh.o_bar));
-            umma_commit_pair(mapa_shared(smem_u32(&sh.o_bar), 1));
-        }
-        flags[0] = ok ? 1 : 0;
-    }
-    __syncwarp();
-    const bool s_ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.s_bar), 0, w, 1u));
-    if (s_ok) {
-        tc_fence_after();
-        uint32_t r[32];
-        for (int c = 0; c < 4; ++c) {
-            tmem_ld32(tmem + lane_off + c * 32, r);
-            tmem_wait_ld();
-            for (int e = 0; e < 32; ++e) {
-                s_out[(rank * 128 + row) * 128 + c * 32 + e] = __uint_as_float(r[e]);
-            }
-        }
-    }
-    const bool o_ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.o_bar), 0, w, 2u));
-    if (o_ok) {
-        tc_fence_after();
-        uint32_t r[32];
-        for (int c = 0; c < 4; ++c) {
-            tmem_ld32(tmem + lane_off + 128 + c * 32, r);
-            tmem_wait_ld();
-            for (int e = 0; e < 32; ++e) {
-                o_out[(rank * 128 + row) * 128 + c * 32 + e] = __uint_as_float(r[e]);
-            }
-        }
-    }
-    if (threadIdx.x == 0 && rank == 1) {
-        flags[2] = (s_ok && o_ok) ? 1 : 0;
-    }
-    tc_fence_before();
-    cluster_sync();
-    if (warp == 0) {
-        tc_fence_after();
-        tmem_dealloc_pair(tmem, 512);
-    }
-    if (threadIdx.x == 0) {
-        flags[1 + 2 * rank] = 1;
-    }
-}
-
 thread_local std::string g_err;
 
 }  // namespace
 }  // namespace fa_sm100
 
 extern "C" {
-
-// CTA-pair probe: q [256][128], k [128][128], v [128][128], p [256][128] fp16 device pointers;
-// s_out [256][128] f32 (S = Q K^T), o_out [256][128] f32 (O = P V), flags [4] int.
-// Synchronises. Returns 0 on success, else a message in fa_selftest_error().
-__attribute__((visibility("default"))) int fa_selftest_umma_pair(const void* q, const void* k, const void* v,
-                                                                 const void* p, float* s_out, float* o_out,
-                                                                 int* flags) {
-    using namespace fa_sm100;
-    CUtensorMap maps[3];
-    if (encode_bhnd_map(&maps[0], q, 1, 256, 128, 128) != CUDA_SUCCESS ||
-        encode_bhnd_map(&maps[1], k, 1, 128, 128, 64) != CUDA_SUCCESS ||
-        encode_bhnd_map(&maps[2], v, 1, 128, 128, 128) != CUDA_SUCCESS) {
-        g_err = "tensor map encoding failed";
-        return 2;
-    }
-    // 160 KB although 64 KB are used: a misread operand layout would still stay inside this
-    // CTA's shared memory.
-    const int smem = 160 * 1024;
-    cudaError_t err = cudaFuncSetAttribute(umma_pair_probe_kernel,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (err == cudaSuccess) {
-        umma_pair_probe_kernel<<<2, 128, smem>>>(maps[0], maps[1], maps[2],
-                                                 static_cast<const __half*>(p), s_out, o_out, flags);
-        err = cudaGetLastError();
-    }
-    if (err == cudaSuccess) {
-        err = cudaDeviceSynchronize();
-    }
-    if (err != cudaSuccess) {
-        g_err = std::string("CUDA error: ") + cudaGetErrorString(err);
-        return 3;
-    }
-    return 0;
-}
 
 // Runs the probe on the current device: q, k, v are [128][d] fp16, p is [128][128] fp16
 // (device pointers); outputs: s_out [128][128] f32, o_out [128][d] f32, o16_raw [128][d] raw

@@ -77,25 +77,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return done != 0;
 }
 
-// try_wait with a suspend-time hint: a thread whose phase is not complete sleeps until the phase
-// completes or about `hint_ns` pass, instead of returning after the system's default limit, so
-// that a waiting warp takes fewer issue slots from the warps sharing its sub-partition.
-__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(bar), "r"(parity), "r"(hint_ns)
-        : "memory");
-    return done != 0;
-}
-
-#ifndef FA_WAIT_SUSPEND_NS
-#define FA_WAIT_SUSPEND_NS 0  // 0: default try_wait limit
-#endif
-
 // Where a bounded wait reports that it gave up.
 struct WaitCtx {
     volatile int* cta_abort;           // shared flag: some thread of this CTA gave up
@@ -120,8 +101,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const W
     const long long t0 = clock64();
     uint32_t spins = 0;
     while (true) {
-        if (FA_WAIT_SUSPEND_NS > 0 ? mbar_try_wait_sleep(bar, parity, FA_WAIT_SUSPEND_NS)
-                                   : mbar_try_wait(bar, parity)) {
+        if (mbar_try_wait(bar, parity)) {
             return true;
         }
         // The abort flag and the clock are checked every 32 polls only: a polling warp shares
@@ -431,113 +411,6 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
 
 __device__ __forceinline__ float2 unpack_half2(uint32_t r) {
     return __half22float2(*reinterpret_cast<const __half2*>(&r));
-}
-
-// ------------------------------------------------------------------------------------------
-// CTA pairs (a cluster of 2 CTAs on 2 SMs sharing one tcgen05.mma, cta_group::2).
-// ------------------------------------------------------------------------------------------
-
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-
-// All threads of both CTAs; release/acquire at cluster scope.
-__device__ __forceinline__ void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// Makes mbarrier initialisation visible to the other CTA of the cluster.
-__device__ __forceinline__ void mbar_fence_init_cluster() {
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-
-// Address of the same shared-memory location in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-    return r;
-}
-
-// Arrival on an mbarrier of any CTA of the cluster (default semantics: release at CTA scope).
-// Used to signal that this thread's tcgen05.st results are in its TMEM (ordered before the
-// arrival by tcgen05.wait::st and tcgen05.fence::before_thread_sync); a release at cluster
-// scope measured ~1000 clk per arrival on B200 and is not needed for that.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-
-// try_wait with acquire at cluster scope (for barriers the other CTA arrives on).
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return done != 0;
-}
-
-// Tensor memory of a CTA pair: one warp of each CTA (same warp index) allocates; both CTAs get
-// the same column address.
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t smem_dst, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_dst),
-                 "r"(ncols)
-                 : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish_pair() {
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
-                 : "memory");
-}
-
-// Bit 24 of a shared::cluster address selects the CTA of a pair: cleared, it names the same
-// offset in the pair's even (leader) CTA.
-constexpr uint32_t kPairLeaderMask = 0xFEFFFFFFu;
-
-// TMA 3-D tiled load into this CTA's shared memory whose completion (transaction bytes) is
-// counted on the pair leader's mbarrier at the same offset as `bar`. No cluster broadcast.
-__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                                 int x, int y, int z) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
-        "[%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar & kPairLeaderMask), "r"(x), "r"(y), "r"(z)
-        : "memory");
-}
-
-// One tcgen05.mma for the CTA pair (M = 256: rows 0..127 in the leader's TMEM, 128..255 in
-// the other CTA's), issued by the leader. A and B descriptors are CTA-local shared-memory
-// addresses, the same offsets in both CTAs; B is split along N between the two CTAs.
-__device__ __forceinline__ void umma_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                             uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-__device__ __forceinline__ void umma_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                             uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-// Arrival on `cluster_bar` (an mbarrier of either CTA, shared::cluster address) once every
-// pair MMA issued so far by this thread has completed.
-__device__ __forceinline__ void umma_commit_pair(uint32_t cluster_bar) {
-    asm volatile(
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)
-        : "memory");
 }
 
 }  // namespace fa_sm100

@@ -1,6 +1,5 @@
 #pragma once
-// Softmax building blocks shared by the forward kernels (flash_fwd_sm100.cu, the one-CTA
-// kernel, and flash_fwd_pair_sm100.cu, the CTA-pair kernel).
+// Softmax building blocks of the forward kernel (flash_fwd_sm100.cu).
 
 #include <cstdint>
 
@@ -35,19 +34,6 @@ __device__ __forceinline__ float row_extreme(const uint32_t (&sr)[N]) {
     }
     return MAX ? fmax3(fmax3(m[0], m[1], m[2]), fmax3(m[3], m[4], m[5]), fmaxf(m[6], m[7]))
                : fmin3(fmin3(m[0], m[1], m[2]), fmin3(m[3], m[4], m[5]), fminf(m[6], m[7]));
-}
-
-// Named barrier `id` over `n` threads: wait (bar.sync) / signal without waiting (bar.arrive).
-__device__ __forceinline__ void named_bar_sync(int id, int n) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
-__device__ __forceinline__ void named_bar_arrive(int id, int n) {
-    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
-
-// Named barrier over the two warps (one per column half) that own the same 32 rows.
-__device__ __forceinline__ void pair_sync(int id) {
-    asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
 }
 
 }  // namespace fa_sm100

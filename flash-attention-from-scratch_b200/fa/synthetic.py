@@ -40,6 +40,30 @@ def make_qkv(
     return q.half(), k.half(), v.half()
 
 
+def make_head_qkv(
+    heads: range,
+    n: int,
+    d: int,
+    seed: int,
+    scale: float = 1.0,
+    outliers: bool = False,
+    outlier_factor: float = 8.0,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """CPU fp16 q, k, v of shape [1, len(heads), n, d]: head h of a workload drawn from its own
+    generator seeded with seed * 65536 + h (q, then k, then v), with the same value scale and
+    outliers as make_qkv. A shard of a workload's heads is generated without drawing the other
+    heads, and a head's values do not depend on how the heads are sharded."""
+    out = [torch.empty(1, len(heads), n, d, dtype=torch.float16) for _ in range(3)]
+    for i, h in enumerate(heads):
+        g = torch.Generator().manual_seed(seed * 65536 + h)
+        for t in out:
+            x = torch.randn(n, d, generator=g) * scale
+            if outliers and t is not out[2]:
+                x[:, : outlier_channels(d)] *= outlier_factor
+            t[0, i] = x.half()
+    return out[0], out[1], out[2]
+
+
 # BASELINE.json configs (shapes, seeds, value scales). cfg0 is the CPU anchor.
 CONFIGS = {
     "cfg0": dict(b=1, h=4, n=512, d=64, causal=False, seed=0, scale=1.0),

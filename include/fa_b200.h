@@ -1,8 +1,11 @@
 /* C ABI of the B200 (sm_100a) FlashAttention-2 forward library, libfa_b200.so.
  *
  * Plain C: raw device pointers, sizes and a CUDA stream handle, no PyTorch or C++ types, so a
- * ctypes / cgo / JNI / N-API binding can call it directly. Every entry point is re-entrant and
- * thread-safe; the library keeps no per-call state and allocates no device memory per call.
+ * ctypes / cgo / JNI / N-API binding can call it directly. The library allocates no device
+ * memory. Every entry point is re-entrant and thread-safe and keeps no per-call state, with one
+ * exception: fa_flash_fwd_splitkv_static shares one fixed scratch per device between its calls
+ * (see its declaration). Device addresses and kernel attributes the library caches are keyed
+ * on the device's current CUDA context, so they are looked up again after a device reset.
  *
  * Reference interfaces each entry point replaces (aligoldenhat/flash-attention-from-scratch):
  *   FaFwdParams          <- fa::FlashFwdParams          csrc/flash_fwd.h:18-30
@@ -110,23 +113,21 @@ FA_API int fa_splitkv_choose(const FaFwdParams* params, int32_t num_sms, int32_t
 FA_API int fa_flash_fwd_splitkv(const FaFwdParams* params, int32_t num_splits, void* workspace,
                                 uint64_t workspace_bytes, fa_stream_t stream);
 
-/* Experimental (no counterpart in the reference): fa_flash_fwd on the CTA-pair kernel, where a
- * cluster of two CTAs on two SMs shares each tcgen05.mma (cta_group::2) and TMEM holds two S
- * and two P buffers, so the next scores are computed during the softmax. head_dim 128,
- * baseline or opt variant only (FA_ERR_INVALID_ARGUMENT otherwise). Same results within the
- * parity tolerance; measured slower than fa_flash_fwd on B200, which therefore does not use it. */
-FA_API int fa_flash_fwd_pair(const FaFwdParams* params, fa_stream_t stream);
-
 /* fa_flash_fwd_splitkv without a caller workspace, allocating nothing (no counterpart in the
- * reference). The split partials go to a fixed scratch of 32 MiB (33554432 bytes) per device,
- * a static __device__ array of the library; a problem whose split-KV workspace
+ * reference), for callers that cannot allocate device memory or hand it over (a runtime whose
+ * allocator is not exposed to the binding, or a host language without CUDA bindings). The
+ * split partials go to a fixed scratch of 32 MiB (33554432 bytes) per device, a static
+ * __device__ array of the library; a problem whose split-KV workspace
  * (fa_splitkv_workspace_size) exceeds it is rejected with FA_ERR_INVALID_ARGUMENT and a
  * message. Nothing in the scratch needs to start at zero: every record a call reads was
- * written by the same call. The first call on each device looks the scratch address up
- * (cudaGetSymbolAddress) and caches it; make that first call outside any stream capture.
- * There is one scratch per device: calls whose work can overlap on the GPU (different streams
- * without ordering between them) race on it and give wrong results; calls on one stream are
- * ordered by the stream. */
+ * written by the same call. The array is in a module of its own: under CUDA's lazy module
+ * loading (the default) a device holds its 32 MiB from the first call of this entry point
+ * there until the process exits; under CUDA_MODULE_LOADING=EAGER every device the library
+ * runs on holds it, whichever entry points are called. The first call on each device (and
+ * the first after a device reset) looks the scratch address up (cudaGetSymbolAddress) and
+ * caches it; make that first call outside any stream capture. There is one scratch per
+ * device: calls whose work can overlap on the GPU (different streams without ordering between
+ * them) race on it and give wrong results; calls on one stream are ordered by the stream. */
 FA_API int fa_flash_fwd_splitkv_static(const FaFwdParams* params, int32_t num_splits,
                                        fa_stream_t stream);
 

@@ -8,6 +8,7 @@ Also exposes ``load_f64()`` returning a callable over numpy arrays.
 from __future__ import annotations
 
 import ctypes
+import hashlib
 import subprocess
 from pathlib import Path
 
@@ -18,12 +19,19 @@ SRC = HERE / "attention_f64.c"
 OUT = HERE / "_build" / "liboracle_f64.so"
 
 
+FLAGS = ["-O2", "-std=c11", "-shared", "-fPIC"]
+
+
 def build(force: bool = False) -> Path:
+    """gcc build of SRC, redone whenever the source or flags differ from the stamped build."""
     OUT.parent.mkdir(parents=True, exist_ok=True)
-    if force or not OUT.exists() or OUT.stat().st_mtime < SRC.stat().st_mtime:
+    digest = hashlib.sha256(" ".join(FLAGS).encode() + b"\0" + SRC.read_bytes()).hexdigest()
+    stamp = OUT.with_name(OUT.name + ".stamp")
+    if force or not OUT.exists() or not stamp.exists() or stamp.read_text().strip() != digest:
         tmp = OUT.with_suffix(".so.tmp")
-        subprocess.run(["gcc", "-O2", "-std=c11", "-shared", "-fPIC", "-o", str(tmp), str(SRC), "-lm"], check=True)
+        subprocess.run(["gcc", *FLAGS, "-o", str(tmp), str(SRC), "-lm"], check=True)
         tmp.replace(OUT)
+        stamp.write_text(digest + "\n")
     return OUT
 
 

@@ -1,6 +1,6 @@
 """Generates the golden attention vectors in tests/golden/ from the REFERENCE's own oracle.
 
-    python tests/golden/make_golden.py /path/to/flash-attention-from-scratch
+    python tests/golden/make_golden.py REFERENCE_DIR     (a checkout of the reference)
 
 Loads ``attention_reference`` from the reference checkout's fa/reference.py by file path
 (importing the package ``fa`` there would need its compiled extension) and runs it on torch
@@ -42,7 +42,9 @@ CASES = [
 
 
 def main() -> None:
-    ref_root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) < 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py REFERENCE_DIR")
+    ref_root = Path(sys.argv[1])
     spec = importlib.util.spec_from_file_location("fa_reference_oracle", ref_root / "fa" / "reference.py")
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)

@@ -1,0 +1,284 @@
+/* Native C caller of libfa_b200.so through its C ABI (include/fa_b200.h) -- TEST
+ * INFRASTRUCTURE: it links the double-precision oracle (oracle/attention_f64.c) as its checker.
+ *
+ * The counterpart of the reference's standalone driver (csrc/dev/main.cu:82-188: seeded
+ * inputs, a launch checked against a double-precision CPU reference, CUDA-event timing and a
+ * TFLOPS line) and of its GoogleTest API suite (tests/cpp/test_flash_fwd.cu:64-83 argument
+ * validation, :115-210 shapes x variants against the CPU reference), written as a plain C
+ * program: no Python, no PyTorch, no C++ -- what a cgo / JNI / N-API binding would do.
+ *
+ *   capi_check                         the built-in case list (exit 0 when every case passes)
+ *   capi_check B H N D CAUSAL VARIANT ITERS     one case, then ITERS timed launches
+ *   capi_check --validate-only         argument validation only (needs no GPU)
+ *
+ * Per case: fp16 inputs from a seeded generator (xorshift64* + Box-Muller), device buffers from
+ * cudaMalloc, fa_flash_fwd on a created stream, the watchdog word, the output against the
+ * oracle (fp32 variants: max-abs <= max(2e-3, fp16 floor + 2.5e-4) and mean-abs <= 2e-4;
+ * fp16acc: max-abs <= 1e-2), and a second launch that must reproduce the output bit for bit.
+ */
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "fa_b200.h"
+
+int oracle_attention_f64(const uint16_t* q, const uint16_t* k, const uint16_t* v, int64_t heads,
+                         int64_t n, int64_t d, int causal, double scale, double* out);
+
+#define CHECK_CUDA(call)                                                                      \
+    do {                                                                                      \
+        cudaError_t e_ = (call);                                                              \
+        if (e_ != cudaSuccess) {                                                              \
+            fprintf(stderr, "%s:%d: %s: %s\n", __FILE__, __LINE__, #call, cudaGetErrorString(e_)); \
+            exit(2);                                                                          \
+        }                                                                                     \
+    } while (0)
+
+static uint64_t rng_state;
+
+static double rng_uniform(void) { /* xorshift64*, 53-bit uniform in (0, 1) */
+    rng_state ^= rng_state >> 12;
+    rng_state ^= rng_state << 25;
+    rng_state ^= rng_state >> 27;
+    const uint64_t r = rng_state * 0x2545F4914F6CDD1DULL;
+    return ((double)(r >> 11) + 0.5) * (1.0 / 9007199254740992.0);
+}
+
+static double rng_normal(void) { /* Box-Muller */
+    const double u = rng_uniform(), w = rng_uniform();
+    return sqrt(-2.0 * log(u)) * cos(6.283185307179586 * w);
+}
+
+/* binary32 -> binary16 bits, round to nearest even (normals, subnormals, overflow to inf). */
+static uint16_t float_to_half_bits(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    const uint16_t sign = (uint16_t)((x >> 16) & 0x8000u);
+    const uint32_t absx = x & 0x7fffffffu;
+    if (absx >= 0x7f800000u) { /* inf / nan */
+        return sign | (absx > 0x7f800000u ? 0x7e00u : 0x7c00u);
+    }
+    if (absx >= 0x477ff000u) { /* rounds to >= 65520: inf */
+        return sign | 0x7c00u;
+    }
+    if (absx < 0x38800000u) { /* below the smallest normal half: subnormal or zero */
+        if (absx < 0x33000000u) {
+            return sign;
+        }
+        const uint32_t man = (absx & 0x7fffffu) | 0x800000u;
+        const int shift = 126 - (int)(absx >> 23); /* 14 .. 24 */
+        uint32_t h = man >> shift;
+        const uint32_t rem = man & ((1u << shift) - 1u), half = 1u << (shift - 1);
+        if (rem > half || (rem == half && (h & 1u))) {
+            ++h;
+        }
+        return sign | (uint16_t)h;
+    }
+    uint32_t h = ((absx - 0x38000000u) >> 13);
+    const uint32_t rem = absx & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) {
+        ++h;
+    }
+    return sign | (uint16_t)h;
+}
+
+static double half_bits_to_double(uint16_t h) {
+    const int exp = (h >> 10) & 0x1f, man = h & 0x3ff;
+    double v = exp == 0 ? ldexp((double)man, -24) : ldexp((double)(man | 0x400), exp - 25);
+    return (h & 0x8000u) ? -v : v;
+}
+
+static double round_to_half(double x) { return half_bits_to_double(float_to_half_bits((float)x)); }
+
+static const char* variant_name(int v) {
+    return v == FA_VARIANT_BASELINE ? "baseline" : v == FA_VARIANT_OPT ? "opt" : "fp16acc";
+}
+
+/* Validation through the C ABI, before any device work (reference tests/cpp/test_flash_fwd.cu:64-83). */
+static int check_validation(void) {
+    FaFwdParams p;
+    memset(&p, 0, sizeof(p));
+    p.q = p.k = p.v = (const void*)0x10000;
+    p.o = (void*)0x20000;
+    p.batch = 1;
+    p.heads = 1;
+    p.seqlen = 64;
+    p.head_dim = 96;
+    p.softmax_scale = 0.1f;
+    p.variant = FA_VARIANT_OPT;
+    int bad = 0;
+    if (fa_flash_fwd(&p, NULL) != FA_ERR_INVALID_ARGUMENT || strstr(fa_last_error(), "head_dim") == NULL) {
+        fprintf(stderr, "validation: head_dim 96 not rejected (%s)\n", fa_last_error());
+        bad = 1;
+    }
+    p.head_dim = 64;
+    p.seqlen = 0;
+    if (fa_flash_fwd(&p, NULL) != FA_ERR_INVALID_ARGUMENT) {
+        fprintf(stderr, "validation: seqlen 0 not rejected\n");
+        bad = 1;
+    }
+    p.seqlen = 64;
+    p.q = (const void*)0x10008;
+    if (fa_flash_fwd(&p, NULL) != FA_ERR_INVALID_ARGUMENT || strstr(fa_last_error(), "aligned") == NULL) {
+        fprintf(stderr, "validation: misaligned q not rejected (%s)\n", fa_last_error());
+        bad = 1;
+    }
+    p.q = (const void*)0x10000;
+    p.variant = 3;
+    if (fa_flash_fwd(&p, NULL) != FA_ERR_INVALID_ARGUMENT || strstr(fa_last_error(), "variant") == NULL) {
+        fprintf(stderr, "validation: variant 3 not rejected (%s)\n", fa_last_error());
+        bad = 1;
+    }
+    printf("validation: %s\n", bad ? "FAILED" : "ok");
+    return bad;
+}
+
+static int run_case(int b, int h, int n, int d, int causal, int variant, int iters, uint64_t seed) {
+    const size_t elems = (size_t)b * h * n * d, bytes = elems * 2;
+    uint16_t* host[3];
+    rng_state = seed * 0x9E3779B97F4A7C15ULL + 1;
+    for (int t = 0; t < 3; ++t) {
+        host[t] = (uint16_t*)malloc(bytes);
+        for (size_t i = 0; i < elems; ++i) {
+            host[t][i] = float_to_half_bits((float)rng_normal());
+        }
+    }
+    void *dq, *dk, *dv, *dout;
+    CHECK_CUDA(cudaMalloc(&dq, bytes));
+    CHECK_CUDA(cudaMalloc(&dk, bytes));
+    CHECK_CUDA(cudaMalloc(&dv, bytes));
+    CHECK_CUDA(cudaMalloc(&dout, bytes));
+    CHECK_CUDA(cudaMemcpy(dq, host[0], bytes, cudaMemcpyHostToDevice));
+    CHECK_CUDA(cudaMemcpy(dk, host[1], bytes, cudaMemcpyHostToDevice));
+    CHECK_CUDA(cudaMemcpy(dv, host[2], bytes, cudaMemcpyHostToDevice));
+    cudaStream_t stream;
+    CHECK_CUDA(cudaStreamCreate(&stream));
+
+    FaFwdParams p;
+    memset(&p, 0, sizeof(p));
+    p.q = dq;
+    p.k = dk;
+    p.v = dv;
+    p.o = dout;
+    p.batch = b;
+    p.heads = h;
+    p.seqlen = n;
+    p.head_dim = d;
+    p.softmax_scale = (float)(1.0 / sqrt((double)d));
+    p.causal = (uint8_t)causal;
+    p.variant = (uint8_t)variant;
+
+    int failed = 0;
+    uint16_t* out = (uint16_t*)malloc(bytes);
+    uint16_t* out2 = (uint16_t*)malloc(bytes);
+    int rc = fa_flash_fwd(&p, (fa_stream_t)stream);
+    if (rc != FA_OK) {
+        fprintf(stderr, "fa_flash_fwd returned %d: %s\n", rc, fa_last_error());
+        exit(1);
+    }
+    CHECK_CUDA(cudaStreamSynchronize(stream));
+    CHECK_CUDA(cudaMemcpy(out, dout, bytes, cudaMemcpyDeviceToHost));
+    rc = fa_flash_fwd(&p, (fa_stream_t)stream);
+    CHECK_CUDA(cudaStreamSynchronize(stream));
+    CHECK_CUDA(cudaMemcpy(out2, dout, bytes, cudaMemcpyDeviceToHost));
+    if (rc != FA_OK || memcmp(out, out2, bytes) != 0) {
+        fprintf(stderr, "repeat launch differs (rc %d)\n", rc);
+        failed = 1;
+    }
+    int dev = 0;
+    uint32_t status = 0;
+    CHECK_CUDA(cudaGetDevice(&dev));
+    if (fa_device_status(dev, 1, &status) != FA_OK || status != 0) {
+        fprintf(stderr, "watchdog status %#x\n", status);
+        failed = 1;
+    }
+
+    double* ref = (double*)malloc(elems * sizeof(double));
+    if (ref == NULL || oracle_attention_f64(host[0], host[1], host[2], (int64_t)b * h, n, d, causal,
+                                            (double)p.softmax_scale, ref) != 0) {
+        fprintf(stderr, "oracle: out of memory\n");
+        exit(2);
+    }
+    double max_abs = 0.0, sum_abs = 0.0, floor_err = 0.0;
+    for (size_t i = 0; i < elems; ++i) {
+        const double e = fabs(half_bits_to_double(out[i]) - ref[i]);
+        const double f = fabs(round_to_half(ref[i]) - ref[i]);
+        max_abs = e > max_abs ? e : max_abs;
+        floor_err = f > floor_err ? f : floor_err;
+        sum_abs += e;
+    }
+    const double mean_abs = sum_abs / (double)elems;
+    const int acc16 = variant == FA_VARIANT_FP16ACC;
+    const double bound = acc16 ? 1e-2 : fmax(2e-3, floor_err + 2.5e-4);
+    if (!(max_abs <= bound) || (!acc16 && !(mean_abs <= 2e-4))) {
+        failed = 1;
+    }
+    printf("B%d H%d N%d D%d %s %-8s max-abs %.3e (bound %.3e, fp16 floor %.3e) mean-abs %.3e %s\n", b, h, n,
+           d, causal ? "causal" : "full  ", variant_name(variant), max_abs, bound, floor_err, mean_abs,
+           failed ? "FAILED" : "ok");
+
+    if (iters > 0 && !failed) {
+        cudaEvent_t e0, e1;
+        CHECK_CUDA(cudaEventCreate(&e0));
+        CHECK_CUDA(cudaEventCreate(&e1));
+        for (int i = 0; i < 3; ++i) {
+            fa_flash_fwd(&p, (fa_stream_t)stream);
+        }
+        CHECK_CUDA(cudaEventRecord(e0, stream));
+        for (int i = 0; i < iters; ++i) {
+            fa_flash_fwd(&p, (fa_stream_t)stream);
+        }
+        CHECK_CUDA(cudaEventRecord(e1, stream));
+        CHECK_CUDA(cudaEventSynchronize(e1));
+        float ms = 0.0f;
+        CHECK_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+        const double flops = 4.0 * b * h * (double)n * n * d / (causal ? 2.0 : 1.0);
+        printf("  %d launches: %.4f ms each, %.1f TFLOPS\n", iters, ms / iters, flops / (ms / iters * 1e-3) / 1e12);
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+    }
+
+    free(ref);
+    free(out);
+    free(out2);
+    for (int t = 0; t < 3; ++t) {
+        free(host[t]);
+    }
+    cudaFree(dq);
+    cudaFree(dk);
+    cudaFree(dv);
+    cudaFree(dout);
+    cudaStreamDestroy(stream);
+    return failed;
+}
+
+int main(int argc, char** argv) {
+    int failed = check_validation();
+    if (argc == 2 && strcmp(argv[1], "--validate-only") == 0) {
+        return failed ? 1 : 0;
+    }
+    if (argc == 8) {
+        failed |= run_case(atoi(argv[1]), atoi(argv[2]), atoi(argv[3]), atoi(argv[4]), atoi(argv[5]),
+                           atoi(argv[6]), atoi(argv[7]), 42);
+    } else if (argc == 1) {
+        static const int cases[][6] = {
+            /* B, H, N, D, causal, variant */
+            {1, 2, 300, 128, 1, FA_VARIANT_OPT},     {2, 3, 257, 64, 0, FA_VARIANT_BASELINE},
+            {1, 2, 1000, 128, 1, FA_VARIANT_FP16ACC}, {1, 1, 1, 64, 0, FA_VARIANT_OPT},
+            {2, 2, 513, 128, 0, FA_VARIANT_OPT},     {1, 3, 640, 64, 1, FA_VARIANT_FP16ACC},
+            {1, 1, 2500, 128, 0, FA_VARIANT_BASELINE},
+        };
+        for (size_t i = 0; i < sizeof(cases) / sizeof(cases[0]); ++i) {
+            const int* c = cases[i];
+            failed |= run_case(c[0], c[1], c[2], c[3], c[4], c[5], 0, 1234 + i);
+        }
+    } else {
+        fprintf(stderr, "usage: %s [B H N D CAUSAL VARIANT ITERS]\n", argv[0]);
+        return 2;
+    }
+    printf("capi_check: %s\n", failed ? "FAILED" : "all cases passed");
+    return failed ? 1 : 0;
+}

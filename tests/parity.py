@@ -4,6 +4,8 @@ fit at once."""
 
 from __future__ import annotations
 
+import warnings
+
 import torch
 
 import fa
@@ -21,6 +23,16 @@ FP16_FLOOR_SLACK = 2.5e-4
 # The reference's own test tolerance (tests/test_flash_fwd.py:12-13).
 REF_ATOL = 1e-2
 REF_RTOL = 1e-2
+
+
+class LiteralBoundMiss(UserWarning):
+    """A fp32-variant case whose max-abs error exceeds the literal north_star bound (2e-3) but
+    stays within fp16_floor + FP16_FLOOR_SLACK. pytest lists every one in its warnings summary,
+    so a run's log names each case that meets only the floor-relative bound."""
+
+
+# (label, max-abs, fp16 floor, mean-abs) of every literal-bound miss in this process.
+LITERAL_MISSES: list[tuple[str, float, float, float]] = []
 
 
 def err_stats(out: torch.Tensor, ref: torch.Tensor) -> tuple[float, float]:
@@ -42,6 +54,16 @@ def check_tolerance(out, ref, variant: str, label: str = "") -> tuple[float, flo
         bound = max(MAX_ABS_FP32, floor + FP16_FLOOR_SLACK)
         assert mx <= bound, f"{label} max-abs {mx:.3e} > {bound:.3e} (fp16 floor {floor:.3e})"
         assert mean <= MEAN_ABS_FP32, f"{label} mean-abs {mean:.3e} > {MEAN_ABS_FP32}"
+        if mx > MAX_ABS_FP32:
+            LITERAL_MISSES.append((label, mx, floor, mean))
+            warnings.warn(
+                LiteralBoundMiss(
+                    f"literal 2e-3 bound missed: {label or 'case'} max-abs {mx:.3e} "
+                    f"(fp16 rounding floor {floor:.3e}, excess over floor {mx - floor:.2e}; "
+                    f"within floor + {FP16_FLOOR_SLACK:.1e}) mean-abs {mean:.2e}"
+                ),
+                stacklevel=2,
+            )
     return mx, mean
 
 

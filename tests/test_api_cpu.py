@@ -74,17 +74,3 @@ def test_forward_host_empty_sequence_needs_no_gpu():
     q = torch.zeros(2, 3, 0, 64, dtype=torch.float16)
     out = fa.forward_host(q, q, q)
     assert out.shape == q.shape
-
-
-def test_pair_entry_rejects_other_shapes_before_any_cuda_call():
-    import ctypes
-
-    from fa import _C
-
-    _C.lib.fa_flash_fwd_pair.argtypes = [ctypes.POINTER(_C.FaFwdParams), ctypes.c_void_p]
-    p = _C.FaFwdParams()
-    p.q, p.k, p.v, p.o = 0x10000, 0x20000, 0x30000, 0x40000
-    p.batch, p.heads, p.seqlen, p.head_dim = 1, 1, 256, 64
-    p.softmax_scale, p.causal, p.variant = 0.125, 0, 1
-    assert _C.lib.fa_flash_fwd_pair(ctypes.byref(p), None) == _C.FA_ERR_INVALID_ARGUMENT
-    assert "head_dim 128" in _C.lib.fa_last_error().decode()

@@ -134,25 +134,3 @@ def test_bounded_wait_times_out_without_fault():
     q, k, v = (t.cuda() for t in make_qkv(1, 1, 64, 64, seed=1))
     assert torch.isfinite(fa.forward(q, k, v)).all()
     assert fa._C.device_status(0, clear=True) == 0
-
-
-def test_umma_pair_probe_exact():
-    """CTA pair (cluster of 2, cta_group::2): S = Q K^T over 256 rows with K split between the
-    two CTAs' shared memory, O = P V with P in each CTA's TMEM and V split by columns; small
-    integers, so every value is exact."""
-    lib = _lib()
-    lib.fa_selftest_umma_pair.argtypes = [ctypes.c_void_p] * 7
-    g = torch.Generator().manual_seed(7)
-    q = torch.randint(-3, 4, (256, 128), generator=g).half().cuda()
-    k = torch.randint(-3, 4, (128, 128), generator=g).half().cuda()
-    v = torch.randint(-3, 4, (128, 128), generator=g).half().cuda()
-    p = torch.randint(-2, 3, (256, 128), generator=g).half().cuda()
-    s_out = torch.zeros(256, 128, dtype=torch.float32, device="cuda")
-    o_out = torch.zeros(256, 128, dtype=torch.float32, device="cuda")
-    flags = torch.zeros(4, dtype=torch.int32, device="cuda")
-    rc = lib.fa_selftest_umma_pair(q.data_ptr(), k.data_ptr(), v.data_ptr(), p.data_ptr(),
-                                   s_out.data_ptr(), o_out.data_ptr(), flags.data_ptr())
-    assert rc == 0, lib.fa_selftest_error()
-    assert flags.tolist() == [1, 1, 1, 1]
-    torch.testing.assert_close(s_out, q.float() @ k.float().T, atol=0, rtol=0)
-    torch.testing.assert_close(o_out, p.float() @ v.float(), atol=0, rtol=0)
