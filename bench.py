@@ -561,9 +561,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
     syn = synthetic()
 
+    def plan_of(qd, causal, variant) -> dict:
+        """The schedule fa.forward runs (fa_plan on this device)."""
+        return _C.plan_params(_C.make_params(qd, qd, qd, qd, causal, 1.0, _C.parse_variant(variant)), 0)
+
     def kernels_per_launch(qd, kd, vd, causal, variant) -> int:
-        params = _C.make_params(qd, kd, vd, qd, causal, 1.0, _C.parse_variant(variant))
-        return 1 if _C.choose_splits(params, dev) == 1 else 2
+        # the attention kernel, plus the combine when the plan splits key ranges
+        return 2 if plan_of(qd, causal, variant)["workspace_bytes"] > 0 else 1
 
     def timed(step, steps: int, warmup: int, sample_clocks: bool):
         """Device time per step (ms) of `step` over exactly `steps` calls after `warmup`,
@@ -629,7 +633,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         t_value = flops_of(tc) / (t_max * 1e-3) / 1e12
         twin = {"workload": tc["name"], "causal": tc["causal"], "value": t_value, "unit": "TFLOPS",
                 "ms_per_step": t_max, "frac": t_value / world / peak, "clocks": t_clocks,
-                "scaling": "strong", "steps": args.steps}
+                "scaling": "strong", "steps": args.steps, "plan_rank0": plan_of(qd, tc["causal"], variant)}
 
     # ---- weak scaling (N > 1): every rank a private copy of config 1 ----
     weak = None
@@ -676,6 +680,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                 "variant": pc["variant"], "outliers": bool(pc.get("outliers")), "value": p_val, "unit": "TFLOPS",
                 "ms_per_step": p_ms, "frac": p_val / peak, "hbm_gbs_algorithmic": io / (p_ms * 1e-3) / 1e9,
                 "kernels_per_launch": kernels_per_launch(pq, pk, pv, pc["causal"], pc["variant"]),
+                "plan": plan_of(pq, pc["causal"], pc["variant"]),
                 "traffic": traffic_per_launch(name), "clocks": p_clocks, "steps": args.steps,
             }
             del pq, pk, pv
@@ -764,6 +769,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                 "kernel": f"fa_fwd_sm100_kernel (smem {smem} B, {threads} threads/CTA), rank 0's shard",
             },
             "clocks": clocks,
+            "plan_rank0": plan_of(qd, causal, variant),
             "gpu_launches": args.steps * kpl * world,
             "noncausal" if causal else "causal": twin,
             "weak_scaling": weak,

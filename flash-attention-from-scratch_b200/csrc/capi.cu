@@ -99,24 +99,30 @@ int validate(const FaFwdParams* p) {
     return FA_OK;
 }
 
+fa_sm100::Plan plan_for(const FaFwdParams* p, int num_splits, int sm_count) {
+    return fa_sm100::make_plan(p->batch * p->heads, p->seqlen, p->head_dim, p->causal != 0, p->variant,
+                               num_splits, num_splits == 0, sm_count);
+}
+
 int launch_one(const FaFwdParams* p, cudaStream_t stream, int num_splits, void* workspace,
                uint64_t workspace_bytes) {
     const int rc = validate(p);
     if (rc != FA_OK) {
         return rc;
     }
-    if (num_splits < 1 || num_splits > kMaxSplits) {
+    if (num_splits < 0 || num_splits > kMaxSplits) {
         return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd_splitkv: num_splits must be in 1 .. 64, got " +
                                                  std::to_string(num_splits));
     }
-    if (num_splits > 1) {
-        const uint64_t need = fa_sm100::splitkv_workspace_bytes(p->batch * p->heads, p->seqlen,
-                                                                p->head_dim, num_splits);
-        if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)) {
-            return fail(FA_ERR_INVALID_ARGUMENT,
-                        "flash_fwd_splitkv: workspace must be 16-byte aligned and hold at least " +
-                            std::to_string(need) + " bytes");
-        }
+    // The workspace is checked before any CUDA call (with explicit splits its size does not
+    // depend on the device; device_sm_count falls back to 148 SMs without a device).
+    const fa_sm100::Plan plan = plan_for(p, num_splits, fa_sm100::device_sm_count());
+    if (plan.workspace_bytes > 0 &&
+        (workspace == nullptr || workspace_bytes < plan.workspace_bytes || !aligned16(workspace))) {
+        return fail(FA_ERR_INVALID_ARGUMENT,
+                    std::string(num_splits == 0 ? "flash_fwd_auto" : "flash_fwd_splitkv") +
+                        ": workspace must be 16-byte aligned and hold at least " +
+                        std::to_string(plan.workspace_bytes) + " bytes");
     }
     int device = 0;
     cudaError_t err = cudaGetDevice(&device);
@@ -145,22 +151,21 @@ int launch_one(const FaFwdParams* p, cudaStream_t stream, int num_splits, void* 
     args.scale_log2 = static_cast<float>(static_cast<double>(p->softmax_scale) * M_LOG2E);
     args.epoch = next_epoch();
     args.status = status;
-    args.num_splits = num_splits;
     args.rows_pad = (p->seqlen + 255) / 256 * 256;
-    if (num_splits > 1) {
-        const uint64_t recs = static_cast<uint64_t>(num_splits) * bh * args.rows_pad;
+    if (plan.workspace_bytes > 0) {
+        const uint64_t records = plan.workspace_bytes / (static_cast<uint64_t>(p->head_dim + 2) * 4u);
         args.ws_o = static_cast<float*>(workspace);
-        args.ws_ml = args.ws_o + recs * p->head_dim;
+        args.ws_ml = args.ws_o + records * p->head_dim;
     }
-    err = fa_sm100::launch_forward(prob, args, stream);
+    err = fa_sm100::launch_forward(prob, args, plan, stream);
     if (err == cudaErrorInvalidValue) {
         return fail(FA_ERR_CUDA, "flash_fwd: cuTensorMapEncodeTiled failed");
     }
     if (err != cudaSuccess) {
         return cuda_fail(err, "kernel launch");
     }
-    if (num_splits > 1) {
-        err = fa_sm100::launch_splitkv_combine(prob, args, stream);
+    if (plan.workspace_bytes > 0) {
+        err = fa_sm100::launch_splitkv_combine(prob, args, plan, stream);
         if (err != cudaSuccess) {
             return cuda_fail(err, "split-KV combine launch");
         }
@@ -269,26 +274,45 @@ int fa_splitkv_choose(const FaFwdParams* params, int32_t num_sms, int32_t* num_s
     if (num_sms <= 0) {
         return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd_splitkv: num_sms must be positive");
     }
-    const int rows_per_cta = fa_sm100::kernel_rows_per_cta(params->head_dim, params->variant);
-    const int64_t ctas = static_cast<int64_t>((params->seqlen + rows_per_cta - 1) / rows_per_cta) *
-                         params->batch * params->heads;
-    const int key_tiles = (params->seqlen + 127) / 128;
-    int splits = 1;
-    if (ctas < num_sms) {
-        splits = static_cast<int>(num_sms / ctas);
-        splits = std::min(splits, std::max(1, key_tiles / 2));
-        splits = std::min(splits, 16);
-        splits = std::max(splits, 1);
-    }
     if (num_splits_out != nullptr) {
-        *num_splits_out = splits;
+        *num_splits_out = fa_capi::plan_for(params, 0, num_sms).num_splits;
     }
     fa_capi::clear_error();
     return FA_OK;
 }
 
+int fa_plan(const FaFwdParams* params, int32_t num_sms, FaPlan* plan_out) {
+    const int rc = validate(params);
+    if (rc != FA_OK) {
+        return rc;
+    }
+    const fa_sm100::Plan p = fa_capi::plan_for(params, 0, num_sms > 0 ? num_sms : fa_sm100::device_sm_count());
+    if (plan_out != nullptr) {
+        plan_out->rows_per_item = p.rows_per_item;
+        plan_out->persistent = p.persistent ? 1 : 0;
+        plan_out->num_splits = p.num_splits;
+        plan_out->tail_blocks = p.tail_blocks;
+        plan_out->tail_splits = p.tail_splits;
+        plan_out->head_groups = p.head_groups;
+        plan_out->items = p.items;
+        plan_out->ctas = p.ctas;
+        plan_out->workspace_bytes = p.workspace_bytes;
+    }
+    fa_capi::clear_error();
+    return FA_OK;
+}
+
+int fa_flash_fwd_auto(const FaFwdParams* params, void* workspace, uint64_t workspace_bytes,
+                      fa_stream_t stream) {
+    return launch_one(params, reinterpret_cast<cudaStream_t>(stream), 0, workspace, workspace_bytes);
+}
+
 int fa_flash_fwd_splitkv(const FaFwdParams* params, int32_t num_splits, void* workspace,
                          uint64_t workspace_bytes, fa_stream_t stream) {
+    if (params != nullptr && validate(params) == FA_OK && (num_splits < 1 || num_splits > fa_capi::kMaxSplits)) {
+        return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd_splitkv: num_splits must be in 1 .. 64, got " +
+                                                 std::to_string(num_splits));
+    }
     return launch_one(params, reinterpret_cast<cudaStream_t>(stream), num_splits, workspace,
                       workspace_bytes);
 }

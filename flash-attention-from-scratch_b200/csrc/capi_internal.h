@@ -27,8 +27,13 @@ bool aligned16(const void* p);
 // The reference's fa::flash_fwd checks (csrc/kernels/flash_fwd.cu:625-652), same messages.
 int validate(const FaFwdParams* p);
 
-// Validates, encodes the tensor maps and enqueues the forward (plus the split-KV combine when
-// num_splits > 1, with `workspace` holding the partials) on `stream`.
+// The schedule for `p` on a GPU with sm_count SMs: num_splits key ranges per row block, or,
+// with num_splits == 0, the library's choice (split-KV for few row blocks, a tail split of the
+// last partial wave).
+fa_sm100::Plan plan_for(const FaFwdParams* p, int num_splits, int sm_count);
+
+// Validates, plans (num_splits as in plan_for), encodes the tensor maps and enqueues the forward
+// plus, when the plan splits key ranges, the combine, with `workspace` holding the partials.
 int launch_one(const FaFwdParams* p, cudaStream_t stream, int num_splits, void* workspace,
                uint64_t workspace_bytes);
 

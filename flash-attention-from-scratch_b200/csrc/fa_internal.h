@@ -25,15 +25,26 @@ struct FwdArgs {
     float scale_log2;     // softmax_scale * log2(e)
     unsigned epoch;       // launch epoch, never 0
     DeviceStatus* status; // per-device watchdog record
-    int head_group;       // causal schedule: heads interleaved in one heavy-first sweep (>= 1)
+    // Causal schedule: the heads are cut into head_groups groups of near-equal size (the first
+    // group_extra groups one head larger); each group's row blocks run longest first.
+    int head_groups;
+    int group_base;       // heads per group: num_bh / head_groups
+    int group_extra;      // num_bh % head_groups
     // Split-KV (num_splits > 1): the work item of key range z covers the z-th of num_splits
     // contiguous ranges of its row block's key tiles and writes, per row, its unnormalised fp32
     // O and (m, l) to the workspace instead of O; a combine kernel merges the ranges.
     int num_splits;       // 1 = no split
     int rows_pad;         // workspace rows per head: ceil(N / 256) * 256
-    float* ws_o;          // [num_splits][num_bh][rows_pad][D] fp32
-    float* ws_ml;         // [num_splits][num_bh][rows_pad][2] fp32: m (log2 units), l
-    int num_items;        // work items (row blocks x heads x key ranges), set by the launcher
+    // Tail split (non-causal, num_splits == 1): items tail_from .. are the last tail_blocks row
+    // blocks (in item order), each cut into tail_splits key ranges that run as separate items
+    // and are merged like split-KV, so that the last partial wave of the grid takes a fraction
+    // of a full item's time. tail_from == num_items: no tail split.
+    int tail_from;
+    int tail_blocks;
+    int tail_splits;
+    float* ws_o;          // split records x D fp32 (see splitkv records in the kernel)
+    float* ws_ml;         // split records x 2 fp32: m (log2 units), l
+    int num_items;        // work items, set by the launcher
     void* o;              // output [num_bh][seqlen][D] fp16, set by the launcher
 };
 
@@ -43,6 +54,32 @@ inline unsigned long long splitkv_workspace_bytes(int num_bh, int seqlen, int he
     const unsigned long long recs = rows * static_cast<unsigned long long>(num_bh) * num_splits;
     return recs * head_dim * 4ull + recs * 2ull * 4ull;
 }
+
+// The schedule of one launch, chosen at run time from (N, d, causal, variant, B * H, SMs):
+// the library's counterpart of the reference's compile-time tile table
+// (csrc/kernels/flash_fwd.cu:596-617), which lists runtime selection as not done
+// (docs/fa3_fa4_techniques.md:29).
+struct Plan {
+    int rows_per_item;    // 128 x query tiles per CTA (the kernel build's NQ)
+    int row_blocks;       // ceil(N / rows_per_item) * B * H
+    bool persistent;      // one CTA per SM walks the items (short rows) vs one CTA per item
+    int num_splits;       // key ranges of every row block (1 = none)
+    int tail_blocks;      // non-causal: row blocks of the last partial wave that are cut ...
+    int tail_splits;      // ... into this many key ranges (0 blocks = none)
+    int head_groups;      // causal: groups of heads swept longest row block first
+    int items;            // work items
+    int ctas;             // CTAs launched
+    unsigned long long workspace_bytes;  // split records (0 when nothing is split)
+};
+
+// The plan for `prob` on a GPU with sm_count SMs. num_splits > 0 forces that many key ranges
+// (no tail split); num_splits == 0 lets the library choose, a tail split included when
+// allow_tail is set.
+Plan make_plan(int num_bh, int seqlen, int head_dim, bool causal, int variant, int num_splits,
+               bool allow_tail, int sm_count);
+
+// SMs of the current device (cached per device).
+int device_sm_count();
 
 // Variant ids as in the reference (csrc/flash_fwd.h:12-16).
 enum : int { kVariantBaseline = 0, kVariantOpt = 1, kVariantFp16Acc = 2 };
@@ -118,13 +155,17 @@ inline cudaError_t ensure_smem_limit(int bytes) {
     return err;
 }
 
-// Launches the split-KV combine: O[bh][row] = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s, fp16.
-cudaError_t launch_splitkv_combine(const FwdProblem& prob, const FwdArgs& args, cudaStream_t stream);
+// Launches the split-KV combine over the rows of every split row block (all of them with
+// num_splits > 1, the tail blocks with a tail split):
+// O[bh][row] = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s, fp16.
+cudaError_t launch_splitkv_combine(const FwdProblem& prob, const FwdArgs& args, const Plan& plan,
+                                   cudaStream_t stream);
 
-// Encodes the TMA tensor maps the chosen kernel needs and launches it on `stream`.
-// Returns cudaSuccess, a CUDA launch error, or cudaErrorInvalidValue if a tensor map could not
-// be encoded.
-cudaError_t launch_forward(const FwdProblem& prob, const FwdArgs& args, cudaStream_t stream);
+// Encodes the TMA tensor maps the chosen kernel needs and launches it on `stream` with the
+// schedule `plan` (its split fields must match args'). Returns cudaSuccess, a CUDA launch
+// error, or cudaErrorInvalidValue if a tensor map could not be encoded.
+cudaError_t launch_forward(const FwdProblem& prob, const FwdArgs& args, const Plan& plan,
+                           cudaStream_t stream);
 
 // Shared-memory bytes and threads per CTA of a kernel instantiation (for reports / tests).
 int kernel_smem_bytes(int head_dim, bool causal, int variant);

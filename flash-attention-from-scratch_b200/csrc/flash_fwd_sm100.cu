@@ -45,7 +45,9 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdint>
+#include <cstdlib>
 
 #include "fa_internal.h"
 #include "sm100_ptx.cuh"
@@ -263,7 +265,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     const int per_split = nb * args.num_bh;           // items per key range
     const int grid_n = static_cast<int>(gridDim.x);
     const int cta = static_cast<int>(blockIdx.x);
-    const bool split = args.num_splits > 1;
     auto item_index = [&](int r) -> int {
         const long long idx = static_cast<long long>(r) * grid_n + ((r & 1) ? (grid_n - 1 - cta) : cta);
         return idx < static_cast<long long>(args.num_items) ? static_cast<int>(idx) : -1;
@@ -271,25 +272,49 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     struct Item {
         int bh;
         int q_row0;
-        int z;         // key range (split-KV), 0 otherwise
-        int kv0;       // first key tile of the range
+        int kv0;       // first key tile of the item's key range
         int n_kv[NQ];  // key tiles query tile t processes, from kv0
         int n_max;
+        bool split;    // the rows' partials go to split records (merged by the combine kernel)
+        long long rec0;  // split record of the item's first row (row 0 of query tile 0)
     };
     auto decode = [&](int idx, Item& it) {
-        it.z = idx / per_split;
-        const int lin = idx - it.z * per_split;
+        // Row block `lin` in item order, key range z of `nsplit`, and its split records.
+        int lin, z, nsplit, p = 0;
+        if (idx >= args.tail_from) {
+            // Tail split: the last tail_blocks row blocks, tail_splits consecutive items each.
+            const int j = idx - args.tail_from;
+            p = j / args.tail_splits;
+            z = j - p * args.tail_splits;
+            lin = args.tail_from + p;
+            nsplit = args.tail_splits;
+        } else {
+            z = idx / per_split;
+            lin = idx - z * per_split;
+            nsplit = args.num_splits;
+        }
         int m_block;
         if constexpr (Cfg::CAUSAL) {
             // A causal row block covers more key tiles the later its rows are. Items run in
             // index order, so the index is mapped to (row block, head) longest first across a
-            // group of args.head_group heads (whose K/V stay resident in L2 together): the short
-            // blocks of every group then fill the gaps the long ones leave, instead of a head's
-            // long block starting last and running alone.
-            const int group = lin / (nb * args.head_group);
-            const int head0 = group * args.head_group;
-            const int heads = min(args.head_group, args.num_bh - head0);
-            const int within = lin - group * nb * args.head_group;
+            // group of heads (whose K/V stay resident in L2 together): the short blocks of
+            // every group then fill the gaps the long ones leave, instead of a head's long
+            // block starting last and running alone. Groups differ in size by one head at most.
+            const int big = args.group_base + 1;
+            const int big_items = args.group_extra * big * nb;
+            int head0, heads, within;
+            if (lin < big_items) {
+                const int g = lin / (big * nb);
+                head0 = g * big;
+                heads = big;
+                within = lin - g * big * nb;
+            } else {
+                const int rest = lin - big_items;
+                const int g = rest / (args.group_base * nb);
+                head0 = args.group_extra * big + g * args.group_base;
+                heads = args.group_base;
+                within = rest - g * args.group_base * nb;
+            }
             it.bh = head0 + within % heads;
             m_block = nb - 1 - within / heads;
         } else {
@@ -306,15 +331,22 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             it.n_max = max(it.n_max, it.n_kv[t]);
         }
         it.kv0 = 0;
-        if (split) {
-            // The block's key tiles [0, n_max) in num_splits contiguous ranges; range z here.
-            const int per = (it.n_max + args.num_splits - 1) / args.num_splits;
-            it.kv0 = it.z * per;
+        it.split = nsplit > 1;
+        it.rec0 = 0;
+        if (it.split) {
+            // The block's key tiles [0, n_max) in nsplit contiguous ranges; range z here.
+            const int per = (it.n_max + nsplit - 1) / nsplit;
+            it.kv0 = z * per;
 #pragma unroll
             for (int t = 0; t < NQ; ++t) {
                 it.n_kv[t] = max(0, min(it.n_kv[t] - it.kv0, per));
             }
             it.n_max = max(0, min(it.n_max - it.kv0, per));
+            // Split records: [num_splits][num_bh][rows_pad] (split-KV) or
+            // [tail_splits][tail_blocks][NQ * 128] (tail split).
+            it.rec0 = idx >= args.tail_from
+                          ? (static_cast<long long>(z) * args.tail_blocks + p) * (NQ * kBM)
+                          : (static_cast<long long>(z) * args.num_bh + it.bh) * args.rows_pad + it.q_row0;
         }
     };
 
@@ -615,14 +647,13 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             }
             Item it;
             decode(idx, it);
-            if (split) {
+            if (it.split) {
                 // Split-KV: the row's unnormalised O over this item's key range and its (m, l) go
                 // to the workspace; a range with no keys for this tile records l = 0, which the
                 // combine skips. Every record of a row that exists (q0 < N) is written, so the
                 // workspace needs no initialisation.
                 if (q0 < n && (ok || nt == 0)) {
-                    const size_t rec =
-                        (static_cast<size_t>(it.z) * args.num_bh + it.bh) * args.rows_pad + grow;
+                    const size_t rec = static_cast<size_t>(it.rec0 + t * kBM + row);
                     float4* dst = reinterpret_cast<float4*>(args.ws_o + rec * D);
                     if (nt > 0) {
 #pragma unroll
@@ -1115,25 +1146,55 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 }
 
 // Split-KV combine (reference: none; Flash-Decoding's merge of per-range softmax partials).
-// One warp per (head, row), lanes over the head dim, splits merged in index order (so the
-// result is deterministic): M = max m_s over splits with l_s > 0, then
+// One warp per output row, lanes over the head dim, ranges merged in index order (so the result
+// is deterministic): M = max m_s over the ranges with l_s > 0, then
 // O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s, rounded to fp16.
+// Rows: with split-KV (tail_blocks == 0) every row of every head, row r of head bh at record
+// bh * rows_pad + r; with a tail split the rows of the tail blocks, row r of tail block p at
+// record p * rows_per_block + r, the block being row block tail_from + p of the non-causal item
+// order (head lin / nb, block lin % nb). Range s adds s * split_stride records.
+struct CombineArgs {
+    const float* ws_o;
+    const float2* ws_ml;
+    __half* o;
+    int n;
+    int num_splits;
+    long long split_stride;  // records per key range
+    long long rows;          // output rows of this launch
+    int tail_blocks;         // 0: split-KV layout
+    int tail_from;
+    int nb;                  // row blocks per head
+    int rows_per_block;
+    int rows_pad;
+};
+
 template <int D>
-__global__ void __launch_bounds__(256) splitkv_combine_kernel(const float* __restrict__ ws_o,
-                                                              const float2* __restrict__ ws_ml,
-                                                              __half* __restrict__ o, int num_bh,
-                                                              int n, int rows_pad, int num_splits) {
+__global__ void __launch_bounds__(256) splitkv_combine_kernel(const CombineArgs a) {
     constexpr int PER = D / 32;  // columns per lane
     const long long item = static_cast<long long>(blockIdx.x) * 8 + threadIdx.x / 32;
     const int lane = static_cast<int>(threadIdx.x) % 32;
-    if (item >= static_cast<long long>(num_bh) * n) {
+    if (item >= a.rows) {
         return;
     }
-    const int bh = static_cast<int>(item / n);
-    const int row = static_cast<int>(item - static_cast<long long>(bh) * n);
+    long long rec0, out_row;
+    if (a.tail_blocks == 0) {
+        const long long bh = item / a.n;
+        rec0 = bh * a.rows_pad + (item - bh * a.n);
+        out_row = item;
+    } else {
+        const long long p = item / a.rows_per_block;
+        const long long lin = a.tail_from + p;
+        const long long bh = lin / a.nb;
+        const long long grow = (lin - bh * a.nb) * a.rows_per_block + (item - p * a.rows_per_block);
+        if (grow >= a.n) {
+            return;
+        }
+        rec0 = item;
+        out_row = bh * a.n + grow;
+    }
     float m_max = -INFINITY;
-    for (int sp = 0; sp < num_splits; ++sp) {
-        const float2 ml = ws_ml[(static_cast<size_t>(sp) * num_bh + bh) * rows_pad + row];
+    for (int sp = 0; sp < a.num_splits; ++sp) {
+        const float2 ml = a.ws_ml[rec0 + sp * a.split_stride];
         if (ml.y > 0.0f) {
             m_max = fmaxf(m_max, ml.x);
         }
@@ -1144,15 +1205,15 @@ __global__ void __launch_bounds__(256) splitkv_combine_kernel(const float* __res
         acc[i] = 0.0f;
     }
     float l = 0.0f;
-    for (int sp = 0; sp < num_splits; ++sp) {
-        const size_t rec = (static_cast<size_t>(sp) * num_bh + bh) * rows_pad + row;
-        const float2 ml = ws_ml[rec];
+    for (int sp = 0; sp < a.num_splits; ++sp) {
+        const long long rec = rec0 + sp * a.split_stride;
+        const float2 ml = a.ws_ml[rec];
         if (!(ml.y > 0.0f)) {
             continue;
         }
         const float w = exp2f(ml.x - m_max);
         l = fmaf(ml.y, w, l);
-        const float* src = ws_o + rec * D + lane * PER;
+        const float* src = a.ws_o + rec * D + lane * PER;
         if constexpr (PER == 4) {
             const float4 v = *reinterpret_cast<const float4*>(src);
             acc[0] = fmaf(v.x, w, acc[0]);
@@ -1166,7 +1227,7 @@ __global__ void __launch_bounds__(256) splitkv_combine_kernel(const float* __res
         }
     }
     const float inv = (l > 0.0f) ? (1.0f / l) : 0.0f;
-    __half* dst = o + (static_cast<size_t>(bh) * n + row) * D + lane * PER;
+    __half* dst = a.o + out_row * D + lane * PER;
     if constexpr (PER == 4) {
         *reinterpret_cast<uint2*>(dst) =
             make_uint2(pack_half2(acc[0] * inv, acc[1] * inv), pack_half2(acc[2] * inv, acc[3] * inv));
@@ -1178,8 +1239,7 @@ __global__ void __launch_bounds__(256) splitkv_combine_kernel(const float* __res
 // ------------------------------------------------------------------------------------------
 // Host-side dispatch
 // ------------------------------------------------------------------------------------------
-// SMs of the current device (cached per device).
-inline int device_sm_count() {
+int device_sm_count() {
     static int counts[64] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
@@ -1195,56 +1255,129 @@ inline int device_sm_count() {
     return c;
 }
 
+// A positive number from the environment, or `fallback`.
+static double env_double(const char* name, double fallback) {
+    const char* v = std::getenv(name);
+    if (v == nullptr) {
+        return fallback;
+    }
+    const double x = std::atof(v);
+    return x > 0.0 ? x : fallback;
+}
+
+Plan make_plan(int num_bh, int seqlen, int head_dim, bool causal, int variant, int num_splits,
+               bool allow_tail, int sm_count) {
+    Plan p{};
+    sm_count = std::max(1, sm_count);
+    p.rows_per_item = kernel_rows_per_cta(head_dim, variant);
+    const long long nb = (seqlen + p.rows_per_item - 1) / p.rows_per_item;
+    const long long row_blocks = nb * num_bh;
+    p.row_blocks = static_cast<int>(std::min<long long>(row_blocks, 0x7fffffffLL));
+    const int key_tiles = (seqlen + kBN - 1) / kBN;
+    // Short rows run on a persistent grid, so that each item's Q load and first S overlap the
+    // previous item's tail (measured: B16 H16 N1000 d128 causal 496 -> 554 TFLOPS); longer rows
+    // one CTA per item (cfg1 N4096: 911 vs 862 persistent).
+    p.persistent = seqlen <= kPersistentMaxN;
+    // Split-KV when the row blocks leave SMs idle (few heads x long rows): about SMs / row
+    // blocks ranges, at least two key tiles each, at most 16.
+    int splits = num_splits;
+    if (splits <= 0) {
+        splits = 1;
+        if (row_blocks < sm_count) {
+            splits = static_cast<int>(sm_count / row_blocks);
+            splits = std::min(splits, std::max(1, key_tiles / 2));
+            splits = std::max(1, std::min(splits, 16));
+        }
+    }
+    p.num_splits = splits;
+    // Tail split (non-causal, whose row blocks all cost the same): when the grid's last wave is
+    // partial and the waves are few, cut the last wave's row blocks into k key ranges so that it
+    // takes about 1/k of a full item. In units of one item: the tail costs
+    // ceil(T k / SMs) waves of pieces of 1/k + 2 / key_tiles (a piece's fixed part, its pipeline
+    // fill and drain and its epilogue, is about two key tiles); k = 1 costs one wave.
+    if (allow_tail && num_splits <= 0 && splits == 1 && !causal) {
+        const long long waves = row_blocks / sm_count;
+        const long long tail = row_blocks % sm_count;
+        if (tail > 0 && waves < 8) {
+            double best = 1.0;
+            int best_k = 1;
+            for (int k = 2; k <= 4 && key_tiles / k >= 8; ++k) {
+                const double piece = 1.0 / k + 2.0 / key_tiles;
+                const double cost = static_cast<double>((tail * k + sm_count - 1) / sm_count) * piece;
+                if (cost < best - 0.05) {
+                    best = cost;
+                    best_k = k;
+                }
+            }
+            if (best_k > 1) {
+                p.tail_blocks = static_cast<int>(tail);
+                p.tail_splits = best_k;
+            }
+        }
+    }
+    // Causal head groups: as many near-equal groups as keep each group's K and V (4 N d bytes
+    // per head) within about 64 MiB of the 126 MB L2; a single group when all of it fits in
+    // 96 MiB, so that few heads (a GPU's shard of a sharded problem) get one longest-first sweep.
+    p.head_groups = 1;
+    if (causal) {
+        // Tuning knobs (MiB): FA_L2_GROUP_MIB, the K/V budget of a group; FA_L2_SINGLE_MIB, the
+        // K/V total up to which all heads form one group.
+        static const double group_mib = env_double("FA_L2_GROUP_MIB", 64.0);
+        static const double single_mib = env_double("FA_L2_SINGLE_MIB", 96.0);
+        const double kv = 4.0 * seqlen * head_dim * static_cast<double>(num_bh);
+        const double mib = 1048576.0;
+        if (kv > single_mib * mib) {
+            p.head_groups = static_cast<int>(std::min<double>(num_bh, std::ceil(kv / (group_mib * mib))));
+        }
+    }
+    const long long items = p.tail_blocks > 0 ? row_blocks + static_cast<long long>(p.tail_blocks) * (p.tail_splits - 1)
+                                              : row_blocks * splits;
+    p.items = static_cast<int>(std::min<long long>(items, 0x7fffffffLL));
+    p.ctas = p.persistent ? static_cast<int>(std::min<long long>(items, sm_count)) : p.items;
+    const unsigned long long rec_bytes = static_cast<unsigned long long>(head_dim + 2) * 4ull;
+    if (p.tail_blocks > 0) {
+        p.workspace_bytes = static_cast<unsigned long long>(p.tail_blocks) * p.tail_splits * p.rows_per_item * rec_bytes;
+    } else if (splits > 1) {
+        p.workspace_bytes = splitkv_workspace_bytes(num_bh, seqlen, head_dim, splits);
+    }
+    return p;
+}
+
 template <int D, bool CAUSAL, int VARIANT>
 cudaError_t launch_cfg(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
-                       const CUtensorMap& tm_o, const FwdArgs& args, cudaStream_t stream) {
+                       const CUtensorMap& tm_o, const FwdArgs& args, const Plan& plan, cudaStream_t stream) {
     using Cfg = FwdCfg<D, CAUSAL, VARIANT>;
     auto* kernel = fa_fwd_sm100_kernel<Cfg>;
     cudaError_t err = ensure_smem_limit<fa_fwd_sm100_kernel<Cfg>>(Cfg::kSmemAlloc);
     if (err != cudaSuccess) {
         return err;
     }
-    const int rows_per_cta = Cfg::NQ * kBM;
-    // Heads per heavy-first sweep of the causal schedule: as many as keep their K and V
-    // (2 * N * D * 2 bytes each) within about 48 MiB of the 126 MB L2.
-    FwdArgs launch_args = args;
-    const double kv_bytes = 4.0 * static_cast<double>(args.seqlen) * D;
-    launch_args.head_group =
-        static_cast<int>(std::min<double>(args.num_bh, std::max(1.0, (48.0 * 1048576.0) / kv_bytes)));
-    // One work item per (row block, head, key range). Short rows (N <= kPersistentMaxN) run
-    // on a persistent grid of one CTA per SM that walks the items, so that each item's Q load
-    // and first S overlap the previous item's tail (measured: B16 H16 N1000 d128 causal 496 ->
-    // 554 TFLOPS); longer rows run one CTA per item (cfg1 N4096: 911 vs 862 persistent).
-    const long long items = static_cast<long long>((args.seqlen + rows_per_cta - 1) / rows_per_cta) *
-                            args.num_bh * (args.num_splits > 1 ? args.num_splits : 1);
-    if (items <= 0 || items > 0x7fffffffLL) {
+    if (plan.items <= 0 || plan.ctas <= 0 || plan.rows_per_item != Cfg::NQ * kBM) {
         return cudaErrorInvalidValue;
     }
-    launch_args.num_items = static_cast<int>(items);
-    const bool persistent = args.seqlen <= kPersistentMaxN;
-    const long long ctas = persistent ? std::min<long long>(items, device_sm_count()) : items;
-    kernel<<<dim3(static_cast<unsigned>(ctas)), Cfg::kThreads, Cfg::kSmemAlloc, stream>>>(tm_q, tm_k, tm_v,
-                                                                                         tm_o, launch_args);
+    kernel<<<dim3(static_cast<unsigned>(plan.ctas)), Cfg::kThreads, Cfg::kSmemAlloc, stream>>>(tm_q, tm_k, tm_v,
+                                                                                              tm_o, args);
     return cudaGetLastError();
 }
 
 template <int D, bool CAUSAL>
 cudaError_t launch_variant(int variant, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                            const CUtensorMap& tm_v, const CUtensorMap& tm_o, const FwdArgs& args,
-                           cudaStream_t stream) {
+                           const Plan& plan, cudaStream_t stream) {
     switch (variant) {
         case kVariantBaseline:
-            return launch_cfg<D, CAUSAL, kVariantBaseline>(tm_q, tm_k, tm_v, tm_o, args, stream);
+            return launch_cfg<D, CAUSAL, kVariantBaseline>(tm_q, tm_k, tm_v, tm_o, args, plan, stream);
         case kVariantOpt:
-            return launch_cfg<D, CAUSAL, kVariantOpt>(tm_q, tm_k, tm_v, tm_o, args, stream);
+            return launch_cfg<D, CAUSAL, kVariantOpt>(tm_q, tm_k, tm_v, tm_o, args, plan, stream);
         case kVariantFp16Acc:
-            return launch_cfg<D, CAUSAL, kVariantFp16Acc>(tm_q, tm_k, tm_v, tm_o, args, stream);
+            return launch_cfg<D, CAUSAL, kVariantFp16Acc>(tm_q, tm_k, tm_v, tm_o, args, plan, stream);
         default:
             return cudaErrorInvalidValue;
     }
 }
 
-cudaError_t launch_forward(const FwdProblem& prob, const FwdArgs& args, cudaStream_t stream) {
+cudaError_t launch_forward(const FwdProblem& prob, const FwdArgs& args, const Plan& plan,
+                           cudaStream_t stream) {
     // This kernel: 128-row boxes for Q, K, V and O.
     CUtensorMap maps[4];
     const void* ptrs[4] = {prob.q, prob.k, prob.v, prob.o};
@@ -1254,18 +1387,26 @@ cudaError_t launch_forward(const FwdProblem& prob, const FwdArgs& args, cudaStre
             return cudaErrorInvalidValue;
         }
     }
-    FwdArgs launch_args = args;
-    launch_args.o = prob.o;
+    FwdArgs a = args;
+    a.o = prob.o;
+    a.num_items = plan.items;
+    a.num_splits = plan.num_splits;
+    a.head_groups = std::max(1, plan.head_groups);
+    a.group_base = prob.num_bh / a.head_groups;
+    a.group_extra = prob.num_bh % a.head_groups;
+    a.tail_blocks = plan.tail_blocks;
+    a.tail_splits = plan.tail_blocks > 0 ? plan.tail_splits : 1;
+    a.tail_from = plan.tail_blocks > 0 ? plan.row_blocks - plan.tail_blocks : plan.items;
     const int variant = prob.variant;
     if (prob.head_dim == 64) {
         return prob.causal
-                   ? launch_variant<64, true>(variant, maps[0], maps[1], maps[2], maps[3], launch_args, stream)
-                   : launch_variant<64, false>(variant, maps[0], maps[1], maps[2], maps[3], launch_args, stream);
+                   ? launch_variant<64, true>(variant, maps[0], maps[1], maps[2], maps[3], a, plan, stream)
+                   : launch_variant<64, false>(variant, maps[0], maps[1], maps[2], maps[3], a, plan, stream);
     }
     if (prob.head_dim == 128) {
         return prob.causal
-                   ? launch_variant<128, true>(variant, maps[0], maps[1], maps[2], maps[3], launch_args, stream)
-                   : launch_variant<128, false>(variant, maps[0], maps[1], maps[2], maps[3], launch_args, stream);
+                   ? launch_variant<128, true>(variant, maps[0], maps[1], maps[2], maps[3], a, plan, stream)
+                   : launch_variant<128, false>(variant, maps[0], maps[1], maps[2], maps[3], a, plan, stream);
     }
     return cudaErrorInvalidValue;
 }
@@ -1294,17 +1435,32 @@ int threads_for(int variant) {
     }
 }
 
-cudaError_t launch_splitkv_combine(const FwdProblem& prob, const FwdArgs& args, cudaStream_t stream) {
-    const long long items = static_cast<long long>(prob.num_bh) * prob.seqlen;
-    const dim3 grid(static_cast<unsigned>((items + 7) / 8));
-    auto* out = static_cast<__half*>(prob.o);
-    const auto* ml = reinterpret_cast<const float2*>(args.ws_ml);
-    if (prob.head_dim == 64) {
-        splitkv_combine_kernel<64><<<grid, 256, 0, stream>>>(args.ws_o, ml, out, prob.num_bh,
-                                                             prob.seqlen, args.rows_pad, args.num_splits);
+cudaError_t launch_splitkv_combine(const FwdProblem& prob, const FwdArgs& args, const Plan& plan,
+                                   cudaStream_t stream) {
+    CombineArgs a{};
+    a.ws_o = args.ws_o;
+    a.ws_ml = reinterpret_cast<const float2*>(args.ws_ml);
+    a.o = static_cast<__half*>(prob.o);
+    a.n = prob.seqlen;
+    a.nb = (prob.seqlen + plan.rows_per_item - 1) / plan.rows_per_item;
+    a.rows_per_block = plan.rows_per_item;
+    a.rows_pad = args.rows_pad;
+    if (plan.tail_blocks > 0) {
+        a.num_splits = plan.tail_splits;
+        a.tail_blocks = plan.tail_blocks;
+        a.tail_from = plan.row_blocks - plan.tail_blocks;
+        a.rows = static_cast<long long>(plan.tail_blocks) * plan.rows_per_item;
+        a.split_stride = a.rows;
     } else {
-        splitkv_combine_kernel<128><<<grid, 256, 0, stream>>>(args.ws_o, ml, out, prob.num_bh,
-                                                              prob.seqlen, args.rows_pad, args.num_splits);
+        a.num_splits = plan.num_splits;
+        a.rows = static_cast<long long>(prob.num_bh) * prob.seqlen;
+        a.split_stride = static_cast<long long>(prob.num_bh) * args.rows_pad;
+    }
+    const dim3 grid(static_cast<unsigned>((a.rows + 7) / 8));
+    if (prob.head_dim == 64) {
+        splitkv_combine_kernel<64><<<grid, 256, 0, stream>>>(a);
+    } else {
+        splitkv_combine_kernel<128><<<grid, 256, 0, stream>>>(a);
     }
     return cudaGetLastError();
 }

@@ -49,6 +49,22 @@ class FaFwdParams(ctypes.Structure):
     ]
 
 
+class FaPlan(ctypes.Structure):
+    """ctypes image of ``FaPlan`` (include/fa_b200.h): the schedule fa_flash_fwd_auto runs."""
+
+    _fields_ = [
+        ("rows_per_item", ctypes.c_int32),
+        ("persistent", ctypes.c_int32),
+        ("num_splits", ctypes.c_int32),
+        ("tail_blocks", ctypes.c_int32),
+        ("tail_splits", ctypes.c_int32),
+        ("head_groups", ctypes.c_int32),
+        ("items", ctypes.c_int32),
+        ("ctas", ctypes.c_int32),
+        ("workspace_bytes", ctypes.c_uint64),
+    ]
+
+
 def _load() -> ctypes.CDLL:
     if not _LIB_PATH.exists():
         raise ImportError(
@@ -85,6 +101,10 @@ def _load() -> ctypes.CDLL:
     lib.fa_flash_fwd_splitkv.argtypes = [
         ctypes.POINTER(FaFwdParams), ctypes.c_int32, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]
     lib.fa_flash_fwd_splitkv.restype = ctypes.c_int
+    lib.fa_plan.argtypes = [ctypes.POINTER(FaFwdParams), ctypes.c_int32, ctypes.POINTER(FaPlan)]
+    lib.fa_plan.restype = ctypes.c_int
+    lib.fa_flash_fwd_auto.argtypes = [ctypes.POINTER(FaFwdParams), ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]
+    lib.fa_flash_fwd_auto.restype = ctypes.c_int
     return lib
 
 
@@ -151,6 +171,26 @@ def choose_splits(params: FaFwdParams, device: torch.device) -> int:
     return int(out.value)
 
 
+def plan_params(params: FaFwdParams, num_sms: int = 0) -> dict:
+    """The schedule the library runs for `params` (fa_plan); num_sms <= 0: the current device."""
+    out = FaPlan()
+    rc = lib.fa_plan(ctypes.byref(params), int(num_sms), ctypes.byref(out))
+    if rc != FA_OK:
+        _raise(rc)
+    return {name: int(getattr(out, name)) for name, _ in FaPlan._fields_}
+
+
+_WORKSPACE: dict[tuple, int] = {}
+
+
+def _auto_workspace_bytes(params: FaFwdParams, device: torch.device) -> int:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    key = (idx, params.batch, params.heads, params.seqlen, params.head_dim, params.causal, params.variant)
+    if key not in _WORKSPACE:
+        _WORKSPACE[key] = plan_params(params, _sm_count(device))["workspace_bytes"]
+    return _WORKSPACE[key]
+
+
 def forward(
     q: torch.Tensor,
     k: torch.Tensor,
@@ -159,8 +199,9 @@ def forward(
     softmax_scale: float | None = None,
     variant: str = "opt",
 ) -> torch.Tensor:
-    """O = softmax(Q K^T * scale) V (reference csrc/bindings.cpp:28-64). The library picks the
-    split-KV count (1 whenever the row blocks already fill the GPU)."""
+    """O = softmax(Q K^T * scale) V (reference csrc/bindings.cpp:28-64), on the library's
+    schedule (fa_flash_fwd_auto: split-KV for few row blocks, a tail split of a partial last
+    wave); the split partials' workspace is a torch allocation on the current stream, like O."""
     return forward_splitkv(q, k, v, causal, softmax_scale, variant, None)
 
 
@@ -174,8 +215,8 @@ def forward_splitkv(
     num_splits: int | None = None,
 ) -> torch.Tensor:
     """forward() with an explicit split-KV count (not in the reference): each row block's key
-    range is cut into ``num_splits`` ranges (None = the library's choice). The workspace is a
-    torch allocation on the current stream, like O itself."""
+    range is cut into ``num_splits`` ranges (None = the library's schedule, fa_flash_fwd_auto).
+    The workspace is a torch allocation on the current stream, like O itself."""
     check_inputs(q, k, v)
     with torch.cuda.device(q.device):
         o = torch.empty_like(q)
@@ -185,8 +226,13 @@ def forward_splitkv(
         if q.shape[2] > 0:
             params = make_params(q, k, v, o, causal, scale, vid)
             stream = torch.cuda.current_stream(q.device).cuda_stream
-            splits = choose_splits(params, q.device) if num_splits is None else int(num_splits)
-            if splits == 1:
+            splits = None if num_splits is None else int(num_splits)
+            if splits is None:
+                nbytes = _auto_workspace_bytes(params, q.device)
+                ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device) if nbytes > 0 else None
+                rc = lib.fa_flash_fwd_auto(ctypes.byref(params), ctypes.c_void_p(ws.data_ptr() if ws is not None else 0),
+                                           nbytes, ctypes.c_void_p(stream))
+            elif splits == 1:
                 rc = lib.fa_flash_fwd(ctypes.byref(params), ctypes.c_void_p(stream))
             else:
                 nbytes = ctypes.c_uint64(0)

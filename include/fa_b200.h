@@ -64,8 +64,8 @@ typedef struct FaFwdParams {
     uint8_t reserved[2];
 } FaFwdParams;
 
-/* Enqueues O = softmax(Q K^T * scale) V on `stream` (current device). Asynchronous: no host
- * synchronisation. Validates like the reference (batch, heads, seqlen > 0; head_dim 64/128;
+/* Enqueues O = softmax(Q K^T * scale) V on `stream` (current device), one range of keys per
+ * row block (fa_flash_fwd_auto may split key ranges). Asynchronous: no host synchronisation. Validates like the reference (batch, heads, seqlen > 0; head_dim 64/128;
  * batch*heads <= 65535; 16-byte aligned pointers; known variant) and returns
  * FA_ERR_INVALID_ARGUMENT with a message in fa_last_error() on failure.
  * Reference: fa::flash_fwd, csrc/kernels/flash_fwd.cu:625-652. */
@@ -112,6 +112,39 @@ FA_API int fa_splitkv_choose(const FaFwdParams* params, int32_t num_sms, int32_t
  * 1 .. 64 or a missing / small / misaligned workspace. */
 FA_API int fa_flash_fwd_splitkv(const FaFwdParams* params, int32_t num_splits, void* workspace,
                                 uint64_t workspace_bytes, fa_stream_t stream);
+
+/* ---- Runtime schedule selection (no counterpart in the reference, whose schedule is a
+ *      compile-time tile table per (d, causal), csrc/kernels/flash_fwd.cu:596-617, and which
+ *      lists runtime selection by sequence length as not done, docs/fa3_fa4_techniques.md:29). */
+
+/* The schedule fa_flash_fwd_auto runs for a problem. */
+typedef struct FaPlan {
+    int32_t rows_per_item;  /* query rows per work item: 128 x query tiles per CTA (256, or 128
+                               for fp16acc at head_dim 128) */
+    int32_t persistent;     /* 1: a grid of one CTA per SM walks the items (short rows);
+                               0: one CTA per item */
+    int32_t num_splits;     /* key ranges of every row block (split-KV); 1 = none */
+    int32_t tail_blocks;    /* non-causal: row blocks of the grid's last partial wave, each cut
+                               into tail_splits key ranges; 0 = none */
+    int32_t tail_splits;
+    int32_t head_groups;    /* causal: groups of heads (near-equal sizes) whose row blocks run
+                               longest first, each group's K and V sized to stay in L2 */
+    int32_t items;          /* work items */
+    int32_t ctas;           /* CTAs launched */
+    uint64_t workspace_bytes; /* device workspace for the split partials (0: none needed) */
+} FaPlan;
+
+/* The schedule for `params` on a GPU with num_sms SMs (num_sms <= 0: the current device's).
+ * Validates like fa_flash_fwd; makes no device allocation and launches nothing. */
+FA_API int fa_plan(const FaFwdParams* params, int32_t num_sms, FaPlan* plan_out);
+
+/* fa_flash_fwd with the library's schedule (fa_plan on the current device): split-KV when the
+ * row blocks leave SMs idle, a tail split of the last partial wave for non-causal problems with
+ * few waves. `workspace`: device memory of at least the plan's workspace_bytes, 16-byte aligned
+ * (may be NULL when that is 0); it needs no initialisation and may be reused once the call's
+ * work on `stream` has completed. Results are deterministic for a given device type. */
+FA_API int fa_flash_fwd_auto(const FaFwdParams* params, void* workspace, uint64_t workspace_bytes,
+                             fa_stream_t stream);
 
 /* fa_flash_fwd_splitkv without a caller workspace, allocating nothing (no counterpart in the
  * reference), for callers that cannot allocate device memory or hand it over (a runtime whose
