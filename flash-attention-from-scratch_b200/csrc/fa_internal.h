@@ -19,17 +19,44 @@ struct DeviceStatus {
     unsigned epoch_aborted;
 };
 
+// n / d by a multiply and a shift, for 0 <= n < 2^31 and 1 <= d < 2^31 (division by an invariant
+// integer, Granlund and Montgomery 1994, theorem 4.2): with l = ceil(log2 d) and
+// m = ceil(2^(31+l) / d) (which fits 32 bits), floor(n / d) = floor(n m / 2^(31+l)).
+// The kernel's work-item decode divides by per-launch constants on the path from one item to
+// the next; this keeps each division to two dependent instructions.
+struct FastDiv {
+    unsigned d;
+    unsigned m;
+    unsigned shift;  // 31 + l
+
+    FastDiv() : d(1), m(1u << 31), shift(31) {}
+    explicit FastDiv(int divisor) {
+        d = divisor > 0 ? static_cast<unsigned>(divisor) : 1u;
+        unsigned l = 0;
+        while ((1ull << l) < d) {
+            ++l;
+        }
+        m = static_cast<unsigned>(((1ull << (31 + l)) + d - 1) / d);
+        shift = 31 + l;
+    }
+    __host__ __device__ __forceinline__ int div(int n) const {
+        return static_cast<int>((static_cast<unsigned long long>(static_cast<unsigned>(n)) * m) >> shift);
+    }
+};
+
 struct FwdArgs {
     int seqlen;           // N (queries == keys)
     int num_bh;           // B * H
     float scale_log2;     // softmax_scale * log2(e)
     unsigned epoch;       // launch epoch, never 0
     DeviceStatus* status; // per-device watchdog record
-    // Causal schedule: the heads are cut into head_groups groups of near-equal size (the first
-    // group_extra groups one head larger); each group's row blocks run longest first.
-    int head_groups;
-    int group_base;       // heads per group: num_bh / head_groups
-    int group_extra;      // num_bh % head_groups
+    // Causal schedule: consecutive groups of head_group heads (the last one may be smaller);
+    // each group's row blocks run longest first.
+    int head_group;
+    // Divisors of the work-item decode, set by the launcher: row blocks per head (nb), items per
+    // key range (nb * num_bh), items per head group (nb * head_group), heads of a full group,
+    // heads of the last group, key ranges of a tail block.
+    FastDiv div_nb, div_per_split, div_group_items, div_group, div_last_group, div_tail;
     // Split-KV (num_splits > 1): the work item of key range z covers the z-th of num_splits
     // contiguous ranges of its row block's key tiles and writes, per row, its unnormalised fp32
     // O and (m, l) to the workspace instead of O; a combine kernel merges the ranges.
@@ -66,7 +93,8 @@ struct Plan {
     int num_splits;       // key ranges of every row block (1 = none)
     int tail_blocks;      // non-causal: row blocks of the last partial wave that are cut ...
     int tail_splits;      // ... into this many key ranges (0 blocks = none)
-    int head_groups;      // causal: groups of heads swept longest row block first
+    int head_groups;      // causal: groups of heads swept longest row block first (equal sizes
+                          // ceil(B * H / head_groups), the last one possibly smaller)
     int items;            // work items
     int ctas;             // CTAs launched
     unsigned long long workspace_bytes;  // split records (0 when nothing is split)

@@ -284,12 +284,12 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         if (idx >= args.tail_from) {
             // Tail split: the last tail_blocks row blocks, tail_splits consecutive items each.
             const int j = idx - args.tail_from;
-            p = j / args.tail_splits;
+            p = args.div_tail.div(j);
             z = j - p * args.tail_splits;
             lin = args.tail_from + p;
             nsplit = args.tail_splits;
         } else {
-            z = idx / per_split;
+            z = args.div_per_split.div(idx);
             lin = idx - z * per_split;
             nsplit = args.num_splits;
         }
@@ -297,28 +297,19 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         if constexpr (Cfg::CAUSAL) {
             // A causal row block covers more key tiles the later its rows are. Items run in
             // index order, so the index is mapped to (row block, head) longest first across a
-            // group of heads (whose K/V stay resident in L2 together): the short blocks of
-            // every group then fill the gaps the long ones leave, instead of a head's long
-            // block starting last and running alone. Groups differ in size by one head at most.
-            const int big = args.group_base + 1;
-            const int big_items = args.group_extra * big * nb;
-            int head0, heads, within;
-            if (lin < big_items) {
-                const int g = lin / (big * nb);
-                head0 = g * big;
-                heads = big;
-                within = lin - g * big * nb;
-            } else {
-                const int rest = lin - big_items;
-                const int g = rest / (args.group_base * nb);
-                head0 = args.group_extra * big + g * args.group_base;
-                heads = args.group_base;
-                within = rest - g * args.group_base * nb;
-            }
-            it.bh = head0 + within % heads;
-            m_block = nb - 1 - within / heads;
+            // group of args.head_group heads (whose K/V stay resident in L2 together): the short
+            // blocks of every group then fill the gaps the long ones leave, instead of a head's
+            // long block starting last and running alone.
+            const int group = args.div_group_items.div(lin);
+            const int head0 = group * args.head_group;
+            const int within = lin - group * nb * args.head_group;
+            const bool last = args.num_bh - head0 < args.head_group;
+            const int heads = last ? args.num_bh - head0 : args.head_group;
+            const int rank = last ? args.div_last_group.div(within) : args.div_group.div(within);
+            it.bh = head0 + within - rank * heads;
+            m_block = nb - 1 - rank;
         } else {
-            it.bh = lin / nb;
+            it.bh = args.div_nb.div(lin);
             m_block = lin - it.bh * nb;
         }
         it.q_row0 = m_block * NQ * kBM;
@@ -1315,9 +1306,10 @@ Plan make_plan(int num_bh, int seqlen, int head_dim, bool causal, int variant, i
             }
         }
     }
-    // Causal head groups: as many near-equal groups as keep each group's K and V (4 N d bytes
-    // per head) within about 64 MiB of the 126 MB L2; a single group when all of it fits in
-    // 96 MiB, so that few heads (a GPU's shard of a sharded problem) get one longest-first sweep.
+    // Causal head groups: ceil(heads / G) heads per group with G the number of groups that keep
+    // each group's K and V (4 N d bytes per head) within about 64 MiB of the 126 MB L2; a single
+    // group when all of it fits in 96 MiB, so that few heads (a GPU's shard of a sharded
+    // problem) get one longest-first sweep.
     p.head_groups = 1;
     if (causal) {
         // Tuning knobs (MiB): FA_L2_GROUP_MIB, the K/V budget of a group; FA_L2_SINGLE_MIB, the
@@ -1327,7 +1319,10 @@ Plan make_plan(int num_bh, int seqlen, int head_dim, bool causal, int variant, i
         const double kv = 4.0 * seqlen * head_dim * static_cast<double>(num_bh);
         const double mib = 1048576.0;
         if (kv > single_mib * mib) {
-            p.head_groups = static_cast<int>(std::min<double>(num_bh, std::ceil(kv / (group_mib * mib))));
+            const int groups = static_cast<int>(std::min<double>(num_bh, std::ceil(kv / (group_mib * mib))));
+            // ceil(heads / groups) heads per group: equal groups whenever they divide evenly
+            const int per_group = (num_bh + groups - 1) / groups;
+            p.head_groups = (num_bh + per_group - 1) / per_group;
         }
     }
     const long long items = p.tail_blocks > 0 ? row_blocks + static_cast<long long>(p.tail_blocks) * (p.tail_splits - 1)
@@ -1391,11 +1386,17 @@ cudaError_t launch_forward(const FwdProblem& prob, const FwdArgs& args, const Pl
     a.o = prob.o;
     a.num_items = plan.items;
     a.num_splits = plan.num_splits;
-    a.head_groups = std::max(1, plan.head_groups);
-    a.group_base = prob.num_bh / a.head_groups;
-    a.group_extra = prob.num_bh % a.head_groups;
+    a.head_group = (prob.num_bh + std::max(1, plan.head_groups) - 1) / std::max(1, plan.head_groups);
+    const int nb = (prob.seqlen + plan.rows_per_item - 1) / plan.rows_per_item;
+    a.div_nb = FastDiv(nb);
+    a.div_per_split = FastDiv(nb * prob.num_bh);
+    a.div_group_items = FastDiv(nb * a.head_group);
+    a.div_group = FastDiv(a.head_group);
+    const int last = prob.num_bh % a.head_group;
+    a.div_last_group = FastDiv(last == 0 ? a.head_group : last);
     a.tail_blocks = plan.tail_blocks;
     a.tail_splits = plan.tail_blocks > 0 ? plan.tail_splits : 1;
+    a.div_tail = FastDiv(a.tail_splits);
     a.tail_from = plan.tail_blocks > 0 ? plan.row_blocks - plan.tail_blocks : plan.items;
     const int variant = prob.variant;
     if (prob.head_dim == 64) {

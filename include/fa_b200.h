@@ -127,7 +127,8 @@ typedef struct FaPlan {
     int32_t tail_blocks;    /* non-causal: row blocks of the grid's last partial wave, each cut
                                into tail_splits key ranges; 0 = none */
     int32_t tail_splits;
-    int32_t head_groups;    /* causal: groups of heads (near-equal sizes) whose row blocks run
+    int32_t head_groups;    /* causal: groups of ceil(B*H / head_groups) heads (the last one may
+                               be smaller) whose row blocks run
                                longest first, each group's K and V sized to stay in L2 */
     int32_t items;          /* work items */
     int32_t ctas;           /* CTAs launched */
