@@ -93,7 +93,7 @@
 #define FA_STAGES_D64 8  // K/V ring slots at d = 64 (16 KB each)
 #endif
 #ifndef FA_REGS_SOFTMAX_D64
-#define FA_REGS_SOFTMAX_D64 0  // d = 64: no setmaxnreg (measured faster)
+#define FA_REGS_SOFTMAX_D64 184  // d = 64: softmax warps' registers (setmaxnreg; 0 = none)
 #endif
 
 namespace fa_sm100 {
