@@ -37,8 +37,8 @@
 //        after PV_t(j), and tcgen05.mma operations of one thread execute in issue order;
 //        (d = 64) its own columns [128 NQ + D NQ + 64 t, +64), so that S_t(j+1) can run while
 //        the softmax of tile j is still computing P_t(j).
-//   T_h  (fp16acc) columns [128 NQ + D NQ + D h, +D): fp16 partial of P.V over keys
-//        [64 h, 64 h + 64) of the current K/V tile.
+//   T_t  (fp16acc) columns [128 NQ + D NQ + D t, +D): fp16 partial of P.V over the current
+//        K/V tile, one value per column; P_t lies over S_t as at d = 128.
 
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -108,20 +108,21 @@ struct FwdCfg {
     static constexpr int D = D_;
     static constexpr bool CAUSAL = CAUSAL_;
     static constexpr int VARIANT = VARIANT_;
-    // fp16acc: P.V accumulated in fp16 per 64 keys, folded into fp32 (reference ACC16), with
-    // two fp16 exponentials per instruction (reference EXP16). Exact max (no lazy rescale).
+    // fp16acc (reference ACC16, flash_fwd.cu:439-470): P.V of each 128-key tile accumulated in
+    // fp16 into a fresh partial T_t, which the softmax folds into the fp32 O_t. Exact max (no
+    // lazy rescale), so p <= 1. P is stored as p * 2^-kAccShift, which bounds |T_t| by
+    // (128 >> kAccShift) * max|V|: the reference's per-tile bound (its tiles hold BC = 32 keys
+    // at d = 64 and 64 at d = 128), so the partial overflows fp16 for no input the reference
+    // accepts. O_t and the row sum carry the same power-of-two factor, which O / l cancels.
     static constexpr bool ACC16 = (VARIANT_ == kVariantFp16Acc);
-    static constexpr bool EXP16 = ACC16;
+    static constexpr int kAccShift = ACC16 ? (D == 64 ? 2 : 1) : 0;
     // Lazy rescale (reference LAZY, flash_fwd.cu:365-376): keep a stale row max until the
     // tile max exceeds it by more than 2^8. Threshold 0 = exact running max.
     static constexpr float kRescaleThreshold = (VARIANT_ == kVariantOpt) ? 8.0f : 0.0f;
-    // Query tiles per CTA. fp16acc at d = 128 needs S + O + 2 T = 512 columns for one tile.
+    // Query tiles per CTA. fp16acc at d = 128 needs S + O + T = 384 columns for one tile.
     static constexpr int NQ = (ACC16 && D == 128) ? 1 : 2;
     static constexpr bool SEP_P = !ACC16 && D == 64;
-    // fp16acc with two tiles (d = 64): T_1 (keys 64..127) lives in S_t's upper 64 columns,
-    // free once the softmax has read S_t and written P_t into the lower 64.
-    static constexpr bool T_HI_IN_S = ACC16 && NQ == 2;
-    static constexpr int kEmuPer8 = ACC16 ? 0 : (D == 128 ? FA_EMU_PER8_D128 : FA_EMU_PER8_D64);
+    static constexpr int kEmuPer8 = (D == 128) ? FA_EMU_PER8_D128 : FA_EMU_PER8_D64;
     static constexpr int kPolyDeg = (D == 128) ? FA_EXP_POLY_DEG_D128 : FA_EXP_POLY_DEG_D64;
     static constexpr int kTileBytes = kBM * D * 2;  // one Q, K, V or O tile (BM == BN)
     static constexpr int kBoxes = D / 64;           // TMA boxes per tile
@@ -135,12 +136,10 @@ struct FwdCfg {
     // Tensor memory columns.
     static constexpr int kTmemS = 0;
     static constexpr int kTmemO = NQ * kBN;
-    static constexpr int kTmemExtra = kTmemO + NQ * D;  // P_t (SEP_P) or T_h (ACC16)
-    static constexpr int kTmemUsed =
-        kTmemExtra + (T_HI_IN_S ? NQ * D : (ACC16 ? 2 * D : (SEP_P ? NQ * 64 : 0)));
-    // fp16acc partials of tile t: T_0 over keys [0, 64), T_1 over keys [64, 128).
-    static constexpr int tmem_t0(int t) { return kTmemExtra + (T_HI_IN_S ? D * t : 0); }
-    static constexpr int tmem_t1(int t) { return T_HI_IN_S ? (kTmemS + kBN * t + 64) : (kTmemExtra + D); }
+    static constexpr int kTmemExtra = kTmemO + NQ * D;  // P_t (SEP_P) or T_t (ACC16)
+    static constexpr int kTmemUsed = kTmemExtra + (ACC16 ? NQ * D : (SEP_P ? NQ * 64 : 0));
+    // fp16acc partial of tile t (fp16 cells, one value per column).
+    static constexpr int tmem_t(int t) { return kTmemExtra + D * t; }
     static constexpr int kTmemCols = 512;
     static_assert(kTmemUsed <= kTmemCols, "tensor memory budget");
     // Warps: NQ softmax warpgroups + one producer/MMA warpgroup.
@@ -157,9 +156,8 @@ struct FwdCfg {
     // 8); with FA_REGS_SOFTMAX != 0 the softmax warpgroups go to that many and the
     // producer/MMA warpgroup gives up the difference.
     static constexpr int kRegsLaunch = ((65536 / kThreads) / 8 * 8) > 255 ? 248 : (65536 / kThreads) / 8 * 8;
-    // fp16acc with two tiles: its softmax (exponentials, then the fold of two fp16 partials)
-    // spills at the launch share of 168, so it takes 200 from the producer/MMA warpgroup.
-    static constexpr int kRegsSoftmax = T_HI_IN_S ? 200 : (D == 64 ? FA_REGS_SOFTMAX_D64 : FA_REGS_SOFTMAX);
+    // fp16acc at d = 64 (exponentials, then the fold of its fp16 partial) takes 200.
+    static constexpr int kRegsSoftmax = (D == 64) ? (ACC16 ? 200 : FA_REGS_SOFTMAX_D64) : FA_REGS_SOFTMAX;
     static constexpr int kRegsOther =
         kRegsSoftmax == 0
             ? kRegsLaunch
@@ -221,19 +219,14 @@ __device__ __forceinline__ void issue_pv_mma_f32(uint32_t tmem_o, uint32_t tmem_
     }
 }
 
-// fp16acc: T_h = P[:, 64h:64h+64] V[64h:64h+64, :] accumulated in fp16, fresh per tile.
+// fp16acc: T = P V over the 128 keys of one tile, accumulated in fp16, fresh per tile.
 template <class Cfg>
-__device__ __forceinline__ void issue_pv_mma_f16(uint32_t tmem_t0, uint32_t tmem_t1, uint32_t tmem_p,
-                                                 uint64_t vd) {
+__device__ __forceinline__ void issue_pv_mma_f16(uint32_t tmem_t, uint32_t tmem_p, uint64_t vd) {
     constexpr uint32_t idesc = make_idesc_f16(kBM, Cfg::D, /*d_f32=*/false, /*b_mn_major=*/true);
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-#pragma unroll
-        for (int k4 = 0; k4 < 4; ++k4) {
-            const int kk = h * 4 + k4;
-            umma_ts(h == 0 ? tmem_t0 : tmem_t1, tmem_p + kk * 8, vd + static_cast<uint64_t>(kk * (2048 >> 4)),
-                    idesc, k4 == 0 ? 0u : 1u);
-        }
+    for (int kk = 0; kk < kBN / 16; ++kk) {
+        umma_ts(tmem_t, tmem_p + kk * 8, vd + static_cast<uint64_t>(kk * (2048 >> 4)), idesc,
+                kk == 0 ? 0u : 1u);
     }
 }
 
@@ -404,8 +397,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         const uint32_t t_o = tmem + lane_off + Cfg::kTmemO + t * D;
         const uint32_t t_p = Cfg::SEP_P ? (tmem + lane_off + Cfg::kTmemExtra + t * 64)
                                         : (tmem + lane_off + Cfg::kTmemS + t * kBN);
-        const uint32_t t_t0 = tmem + lane_off + Cfg::tmem_t0(t);
-        const uint32_t t_t1 = tmem + lane_off + Cfg::tmem_t1(t);
+        const uint32_t t_t = tmem + lane_off + Cfg::tmem_t(t);
         const uint32_t bar_s = smem_u32(&sb.s_full[t]);
         const uint32_t bar_sf = smem_u32(&sb.s_free[t]);
         const uint32_t bar_p = smem_u32(&sb.p_full[t]);
@@ -508,7 +500,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 
                 // Probabilities, packed fp16 pairs, into P_t.
                 const float2 mul2 = make_float2(mul, mul);
-                const float2 neg2 = make_float2(-max_used, -max_used);
+                // fp16acc stores p * 2^-kAccShift: the shift joins the max in the exponent.
+                const float neg = (Cfg::kAccShift != 0) ? -max_used - static_cast<float>(Cfg::kAccShift) : -max_used;
+                const float2 neg2 = make_float2(neg, neg);
                 float2 sum2[4];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
@@ -521,15 +515,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     for (int i = 0; i < 32; ++i) {
                         const int c = chunk * 64 + 2 * i;
                         const float2 x2 = __ffma2_rn(make_float2(u2f(sr[c]), u2f(sr[c + 1])), mul2, neg2);
-                        uint32_t h;
-                        if constexpr (Cfg::EXP16) {
-                            h = ex2_approx_f16x2(pack_half2(x2.x, x2.y));
-                        } else {
-                            const float2 e = ((i % 8) < Cfg::kEmuPer8)
-                                                 ? (Cfg::kPolyDeg == 3 ? exp2_poly2_deg3(x2) : exp2_poly2(x2))
-                                                 : make_float2(ex2_approx(x2.x), ex2_approx(x2.y));
-                            h = pack_half2(e.x, e.y);
-                        }
+                        const float2 e = ((i % 8) < Cfg::kEmuPer8)
+                                             ? (Cfg::kPolyDeg == 3 ? exp2_poly2_deg3(x2) : exp2_poly2(x2))
+                                             : make_float2(ex2_approx(x2.x), ex2_approx(x2.y));
+                        const uint32_t h = pack_half2(e.x, e.y);
                         // The row sum adds the fp16-rounded values the MMA consumes, so that O
                         // is normalised by the weights it was accumulated with. (The reference
                         // sums the fp32 values, csrc/kernels/flash_fwd.cu:403-417; measured here
@@ -588,41 +577,33 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     if (lane == 0) {
                         mbar_arrive(bar_p);
                     }
-                    // Fold this tile's two fp16 partials into the fp32 accumulator:
-                    // O = alpha * O + T_0 + T_1.
+                    // Fold this tile's fp16 partial into the fp32 accumulator: O = alpha * O + T.
+                    // T lies in its own columns, so the next S_t (issued right after this P.V)
+                    // runs meanwhile; the next P.V overwrites T only after this warp's next P
+                    // arrival, which follows the fold.
                     ok = __all_sync(0xffffffffu, mbar_wait(bar_o, gj & 1, wctx, kStatusTimeoutSoftmax));
                     if (!ok) {
                         continue;
                     }
                     tc_fence_after();
-                    // One 32-column chunk at a time (three 32-register loads in flight).
+                    // One 32-column chunk at a time (two 32-register loads in flight).
 #pragma unroll 1
                     for (int c = 0; c < D / 32; ++c) {
                         uint32_t a[32];
-                        uint32_t b[32];
                         uint32_t o[32];
-                        tmem_ld32(t_t0 + c * 32, a);
-                        tmem_ld32(t_t1 + c * 32, b);
+                        tmem_ld32(t_t + c * 32, a);
                         if (j > 0) {
                             tmem_ld32(t_o + c * 32, o);
                         }
                         tmem_wait_ld();
 #pragma unroll
                         for (int e = 0; e < 32; ++e) {
-                            const float v = f16cell_to_float(a[e]) + f16cell_to_float(b[e]);
+                            const float v = f16cell_to_float(a[e]);
                             o[e] = f2u(j > 0 ? fmaf(u2f(o[e]), alpha, v) : v);
                         }
                         tmem_st32(t_o + c * 32, o);
                     }
                     tmem_wait_st();
-                    if constexpr (Cfg::T_HI_IN_S) {
-                        // T_1 has been read out of S_t's columns: the next S_t may overwrite them.
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) {
-                            mbar_arrive(bar_sf);
-                        }
-                    }
                 }
             }
 
@@ -861,9 +842,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     ok = mbar_wait(smem_u32(&sb.kv_full[k_slot % STAGES]), (k_slot / STAGES) & 1, wctx,
                                    kStatusTimeoutMma);
                     if (ok && n_t > 0) {
-                        if constexpr (Cfg::SEP_P || Cfg::T_HI_IN_S) {
-                            // The softmax has the previous item's last S_t in registers (and,
-                            // with fp16acc, has folded the T_1 kept in S_t's upper columns).
+                        if constexpr (Cfg::SEP_P) {
+                            // The softmax has the previous item's last S_t in registers.
                             if (s_cnt > 0) {
                                 ok = mbar_wait(smem_u32(&sb.s_free[t]), (s_cnt - 1) & 1, wctx,
                                                kStatusTimeoutMma);
@@ -920,8 +900,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                         }
                         tc_fence_after();
                         if constexpr (Cfg::ACC16) {
-                            issue_pv_mma_f16<Cfg>(tmem + Cfg::tmem_t0(t), tmem + Cfg::tmem_t1(t), p_addr,
-                                                  vd0 + stage_off(vs));
+                            issue_pv_mma_f16<Cfg>(tmem + Cfg::tmem_t(t), p_addr, vd0 + stage_off(vs));
                         } else {
                             issue_pv_mma_f32<Cfg>(o_addr, p_addr, vd0 + stage_off(vs), j == 0);
                         }
@@ -929,14 +908,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                         ++pv_cnt;
                         if constexpr (!Cfg::SEP_P) {
                             // S_t(j+1) reuses the columns P_t(j) was read from by the MMAs above
-                            // (tcgen05.mma operations of one thread execute in issue order); with
-                            // fp16acc also those of T_1, once the softmax has folded it into O.
+                            // (tcgen05.mma operations of one thread execute in issue order).
                             if (next_s) {
-                                if constexpr (Cfg::T_HI_IN_S) {
-                                    ok = mbar_wait(smem_u32(&sb.s_free[t]), (s_cnt - 1) & 1, wctx,
-                                                   kStatusTimeoutMma);
-                                }
-                                ok = ok && mbar_wait(smem_u32(&sb.kv_full[ks]), (k_slot / STAGES) & 1, wctx,
+                                ok = mbar_wait(smem_u32(&sb.kv_full[ks]), (k_slot / STAGES) & 1, wctx,
                                                      kStatusTimeoutMma);
                                 if (!ok) {
                                     break;
@@ -1000,7 +974,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             }
             // Issues the next S_t (K tile in ring slot ks) once its columns are free.
             auto issue_s = [&](int t, int ks, bool last_of_item) -> bool {
-                if constexpr (Cfg::SEP_P || Cfg::T_HI_IN_S) {
+                if constexpr (Cfg::SEP_P) {
                     if (s_cnt[t] > 0 &&
                         !mbar_wait(smem_u32(&sb.s_free[t]), (s_cnt[t] - 1) & 1, wctx, kStatusTimeoutMma)) {
                         return false;
@@ -1087,7 +1061,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                         tc_fence_after();
                         const uint64_t vd = vd0 + stage_off(vs);
                         if constexpr (Cfg::ACC16) {
-                            issue_pv_mma_f16<Cfg>(tmem + Cfg::tmem_t0(t), tmem + Cfg::tmem_t1(t), s_addr, vd);
+                            issue_pv_mma_f16<Cfg>(tmem + Cfg::tmem_t(t), s_addr, vd);
                         } else if constexpr (Cfg::SEP_P) {
                             issue_pv_mma_f32<Cfg>(tmem + Cfg::kTmemO + t * Cfg::D,
                                                   tmem + Cfg::kTmemExtra + t * 64, vd, j == 0);
@@ -1097,8 +1071,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                         umma_commit(smem_u32(&sb.o_done[t]));
                         ++pv_cnt[t];
                         if constexpr (!Cfg::SEP_P) {
-                            // S_t(j+1) reuses the columns P_t(j) was read from by the MMAs above;
-                            // with fp16acc also those of T_1, once the softmax has folded it.
+                            // S_t(j+1) reuses the columns P_t(j) was read from by the MMAs above.
                             if (next_s) {
                                 if (!k_ready) {
                                     ok = mbar_wait(smem_u32(&sb.kv_full[ks]), (k_slot / STAGES) & 1,

@@ -389,13 +389,6 @@ __device__ __forceinline__ float fmin3(float a, float b, float c) {
     return d;
 }
 
-// Two 2^x of packed fp16 values in one instruction.
-__device__ __forceinline__ uint32_t ex2_approx_f16x2(uint32_t x) {
-    uint32_t y;
-    asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
-    return y;
-}
-
 // lo_acc += low half of h, hi_acc += high half of h (fp16 -> fp32 exactly, then an fp32 add).
 __device__ __forceinline__ void add_f16x2_to_f32(float& lo_acc, float& hi_acc, uint32_t h) {
     asm("{\n\t.reg .b16 l, u;\n\tmov.b32 {l, u}, %2;\n\t"

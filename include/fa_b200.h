@@ -44,7 +44,7 @@ typedef struct CUstream_st* fa_stream_t;
 /* Kernel builds (reference csrc/flash_fwd.h:12-16). */
 #define FA_VARIANT_BASELINE 0 /* exact running max, fp32 accumulation                      */
 #define FA_VARIANT_OPT 1      /* lazy rescale (threshold 2^8), fp32 accumulation (default)  */
-#define FA_VARIANT_FP16ACC 2  /* P.V accumulated in fp16 per 64 keys, folded into fp32      */
+#define FA_VARIANT_FP16ACC 2  /* P.V accumulated in fp16 per key tile, folded into fp32     */
 
 /* Forward parameters (reference fa::FlashFwdParams, csrc/flash_fwd.h:18-30).
  * q, k, v, o: [batch, heads, seqlen, head_dim] fp16, contiguous, 16-byte aligned, on the
