@@ -119,8 +119,12 @@ struct FwdCfg {
     // Lazy rescale (reference LAZY, flash_fwd.cu:365-376): keep a stale row max until the
     // tile max exceeds it by more than 2^8. Threshold 0 = exact running max.
     static constexpr float kRescaleThreshold = (VARIANT_ == kVariantOpt) ? 8.0f : 0.0f;
-    // Query tiles per CTA. fp16acc at d = 128 needs S + O + T = 384 columns for one tile.
+    // Query tiles per CTA. fp16acc at d = 128 needs S + O + T = 384 columns for one tile; it
+    // spends the remaining 128 on a second S buffer (kSBufs): S(j+1) is computed while the
+    // softmax works on tile j, and the fold of T(j) waits until the end of tile j+1, so no
+    // tile waits for the previous tile's P.V.
     static constexpr int NQ = (ACC16 && D == 128) ? 1 : 2;
+    static constexpr int kSBufs = (ACC16 && NQ == 1) ? 2 : 1;
     static constexpr bool SEP_P = !ACC16 && D == 64;
     static constexpr int kEmuPer8 = (D == 128) ? FA_EMU_PER8_D128 : FA_EMU_PER8_D64;
     static constexpr int kPolyDeg = (D == 128) ? FA_EXP_POLY_DEG_D128 : FA_EXP_POLY_DEG_D64;
@@ -135,7 +139,7 @@ struct FwdCfg {
     static constexpr int kSmemAlloc = kSmemBytes + 1024;
     // Tensor memory columns.
     static constexpr int kTmemS = 0;
-    static constexpr int kTmemO = NQ * kBN;
+    static constexpr int kTmemO = NQ * kSBufs * kBN;
     static constexpr int kTmemExtra = kTmemO + NQ * D;  // P_t (SEP_P) or T_t (ACC16)
     static constexpr int kTmemUsed = kTmemExtra + (ACC16 ? NQ * D : (SEP_P ? NQ * 64 : 0));
     // fp16acc partial of tile t (fp16 cells, one value per column).
@@ -350,6 +354,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             // thread: 128 arrivals on one barrier word serialise in the shared-memory atomics.
             mbar_init(smem_u32(&sb.s_free[t]), 4);
             mbar_init(smem_u32(&sb.p_full[t]), 4);
+            if (Cfg::kSBufs == 2) {
+                mbar_init(smem_u32(&sb.s_full[1]), 1);  // second S buffer (NQ = 1)
+            }
             mbar_init(smem_u32(&sb.o_done[t]), 1);
             mbar_init(smem_u32(&sb.epi[t]), 4);
         }
@@ -406,6 +413,27 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         // With P in its own columns the wait for the previous P.V is deferred to the first P
         // store, so the exponentials of the first chunk overlap that P.V.
         constexpr bool kLateWait = Cfg::SEP_P;
+        // fp16acc: O_t = a * O_t + T_t (or O_t = T_t for a tile's first key tile), one
+        // 32-column chunk at a time (two 32-register loads in flight).
+        auto fold_t = [&](float a, bool first) {
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+                uint32_t tv[32];
+                uint32_t o[32];
+                tmem_ld32(t_t + c * 32, tv);
+                if (!first) {
+                    tmem_ld32(t_o + c * 32, o);
+                }
+                tmem_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    const float v = f16cell_to_float(tv[e]);
+                    o[e] = f2u(first ? v : fmaf(u2f(o[e]), a, v));
+                }
+                tmem_st32(t_o + c * 32, o);
+            }
+            tmem_wait_st();
+        };
 
         int g0 = 0;  // S / P / P.V count of this tile before the current item
         bool ok = true;
@@ -433,10 +461,18 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 
             float row_max = -INFINITY;  // running max of the scaled scores (log2 units)
             float row_sum = 0.0f;       // running sum of this thread's fp16-rounded probabilities
+            float alpha_prev = 1.0f;    // two S buffers: the rescale of the fold still pending
 
             for (int j = 0; j < nt; ++j) {
                 const int gj = g0 + j;  // running index of S_t(j), P_t(j) and P.V_t(j)
-                ok = ok && __all_sync(0xffffffffu, mbar_wait(bar_s, gj & 1, wctx, kStatusTimeoutSoftmax));
+                // Two S buffers (kSBufs): S(j) in buffer gj & 1, whose barrier completes every
+                // other S.
+                const uint32_t s_off = (Cfg::kSBufs == 2) ? static_cast<uint32_t>((gj & 1) * kBN) : 0u;
+                ok = ok && __all_sync(0xffffffffu,
+                                      (Cfg::kSBufs == 2)
+                                          ? mbar_wait(smem_u32(&sb.s_full[gj & 1]), (gj >> 1) & 1, wctx,
+                                                      kStatusTimeoutSoftmax)
+                                          : mbar_wait(bar_s, gj & 1, wctx, kStatusTimeoutSoftmax));
                 if (!ok) {
                     continue;
                 }
@@ -444,7 +480,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 uint32_t sr[NC];
 #pragma unroll
                 for (int c = 0; c < NC / 32; ++c) {
-                    tmem_ld32(t_s + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+                    tmem_ld32(t_s + s_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
                 }
                 tmem_wait_ld();
                 if constexpr (Cfg::SEP_P) {
@@ -536,7 +572,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                         }
                     }
                     if (ok) {
-                        tmem_st32(t_p + chunk * 32, pk);
+                        tmem_st32(t_p + s_off + chunk * 32, pk);
                     }
                 }
                 if (!ok) {
@@ -570,6 +606,25 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     if (lane == 0) {
                         mbar_arrive(bar_p);
                     }
+                } else if constexpr (Cfg::kSBufs == 2) {
+                    // Fold the previous tile's partial now, while S(j+1) is ready in the other
+                    // buffer: P.V(j) overwrites T only after this tile's P arrival below.
+                    if (j > 0) {
+                        ok = __all_sync(0xffffffffu,
+                                        mbar_wait(bar_o, (gj - 1) & 1, wctx, kStatusTimeoutSoftmax));
+                        if (!ok) {
+                            continue;
+                        }
+                        tc_fence_after();
+                        fold_t(alpha_prev, j == 1);
+                    }
+                    alpha_prev = alpha;
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(bar_p);
+                    }
                 } else {
                     tmem_wait_st();
                     tc_fence_before();
@@ -586,24 +641,18 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                         continue;
                     }
                     tc_fence_after();
-                    // One 32-column chunk at a time (two 32-register loads in flight).
-#pragma unroll 1
-                    for (int c = 0; c < D / 32; ++c) {
-                        uint32_t a[32];
-                        uint32_t o[32];
-                        tmem_ld32(t_t + c * 32, a);
-                        if (j > 0) {
-                            tmem_ld32(t_o + c * 32, o);
-                        }
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int e = 0; e < 32; ++e) {
-                            const float v = f16cell_to_float(a[e]);
-                            o[e] = f2u(j > 0 ? fmaf(u2f(o[e]), alpha, v) : v);
-                        }
-                        tmem_st32(t_o + c * 32, o);
+                    fold_t(alpha, j == 0);
+                }
+            }
+            if constexpr (Cfg::kSBufs == 2) {
+                // The last tile's partial.
+                if (ok && nt > 0) {
+                    ok = __all_sync(0xffffffffu,
+                                    mbar_wait(bar_o, (g0 + nt - 1) & 1, wctx, kStatusTimeoutSoftmax));
+                    if (ok) {
+                        tc_fence_after();
+                        fold_t(alpha_prev, nt == 1);
                     }
-                    tmem_wait_st();
                 }
             }
 
@@ -947,7 +996,89 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             mbar_wait_drain(smem_u32(&sb.mma_idle), 0, wctx, kStatusTimeoutTeardown);
         }
         __syncwarp();
-    } else if (Cfg::kIssuers == 1 && warp == Cfg::kMmaWarp) {
+    } else if (Cfg::kSBufs == 2 && warp == Cfg::kMmaWarp) {
+        // ================= MMA issuer: one query tile, two S buffers (fp16acc) =================
+        // S(i) goes to buffer (running S count) & 1. Per item S(0) and S(1) are issued at
+        // once; after P.V(j) (which reads P(j) from S(j)'s buffer) comes S(j+2) into that same
+        // buffer, in issue order. K_i and V_i are loads 2i and 2i+1 of the item's share of the
+        // producer's sequence; each slot is released after its MMA (slots alternate K / V,
+        // so every slot's releases follow its loads in order).
+        if (lane == 0) {
+            bool ok = true;
+            const uint32_t kv_addr0 = smem_base + Cfg::kSmemKV;
+            const uint64_t qd = make_desc_kmajor_sw128(smem_base + Cfg::kSmemQ);
+            const uint64_t kd0 = make_desc_kmajor_sw128(kv_addr0);
+            const uint64_t vd0 = make_desc_mnmajor_sw128(kv_addr0, kBoxBytes);
+            auto stage_off = [](int stage) -> uint64_t {
+                return static_cast<uint64_t>(stage * (Cfg::kTileBytes >> 4));
+            };
+            auto wait_load = [&](int load) -> bool {
+                return mbar_wait(smem_u32(&sb.kv_full[load % STAGES]), (load / STAGES) & 1, wctx,
+                                 kStatusTimeoutMma);
+            };
+            int ring = 0;    // producer loads of the items before the current one
+            int q_uses = 0;  // Q loads consumed
+            int s_cnt = 0;   // S MMAs issued
+            int pv_cnt = 0;  // P consumed (P.V issued)
+            auto issue_s = [&](int load, bool last_of_item) {
+                const int buf = s_cnt & 1;
+                tc_fence_after();
+                issue_s_mma<Cfg>(tmem + Cfg::kTmemS + buf * kBN, qd, kd0 + stage_off(load % STAGES));
+                umma_commit(smem_u32(&sb.s_full[buf]));
+                umma_commit(smem_u32(&sb.kv_empty[load % STAGES]));
+                if (last_of_item) {
+                    umma_commit(smem_u32(&sb.q_empty[0]));  // Q read for the last time
+                }
+                ++s_cnt;
+            };
+            for (int r = 0; ok; ++r) {
+                const int idx = item_index(r);
+                if (idx < 0) {
+                    break;
+                }
+                Item it;
+                decode(idx, it);
+                const int nk = it.n_kv[0];  // == it.n_max with one query tile
+                const int base = ring;
+                ring += 2 * it.n_max;
+                if (nk == 0) {
+                    continue;
+                }
+                ok = mbar_wait(smem_u32(&sb.q_full[0]), q_uses & 1, wctx, kStatusTimeoutMma);
+                ++q_uses;
+                for (int i = 0; ok && i < min(nk, 2); ++i) {
+                    ok = wait_load(base + 2 * i);
+                    if (ok) {
+                        issue_s(base + 2 * i, i == nk - 1);
+                    }
+                }
+                for (int j = 0; ok && j < nk; ++j) {
+                    const int v_load = base + 2 * j + 1;
+                    ok = mbar_wait(smem_u32(&sb.p_full[0]), pv_cnt & 1, wctx, kStatusTimeoutMma) &&
+                         wait_load(v_load);
+                    if (!ok) {
+                        break;
+                    }
+                    tc_fence_after();
+                    issue_pv_mma_f16<Cfg>(tmem + Cfg::tmem_t(0), tmem + Cfg::kTmemS + (pv_cnt & 1) * kBN,
+                                          vd0 + stage_off(v_load % STAGES));
+                    umma_commit(smem_u32(&sb.o_done[0]));
+                    umma_commit(smem_u32(&sb.kv_empty[v_load % STAGES]));
+                    ++pv_cnt;
+                    if (j + 2 < nk) {
+                        ok = wait_load(base + 2 * (j + 2));
+                        if (ok) {
+                            issue_s(base + 2 * (j + 2), j + 2 == nk - 1);
+                        }
+                    }
+                }
+            }
+            // Every MMA issued above must be complete before tensor memory is released.
+            umma_commit(smem_u32(&sb.mma_idle));
+            mbar_wait_drain(smem_u32(&sb.mma_idle), 0, wctx, kStatusTimeoutTeardown);
+        }
+        __syncwarp();
+    } else if (Cfg::kIssuers == 1 && Cfg::kSBufs == 1 && warp == Cfg::kMmaWarp) {
         // ================================== MMA issuer ====================================
         if (lane == 0) {
             bool ok = true;
