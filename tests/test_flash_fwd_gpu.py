@@ -92,6 +92,22 @@ def test_fp16acc_large_values_no_overflow(causal):
     torch.testing.assert_close(out.float().cpu(), ref, atol=100.0 * REF_ATOL, rtol=REF_RTOL)
 
 
+@pytest.mark.parametrize("d", [64, 128])
+def test_fp16acc_partial_within_reference_bound(d):
+    """q = 0 makes every p = 1; V = 1000 everywhere. The reference's fp16 partial over one key
+    tile of BC keys reaches BC * 1000 (BC = 32 at d = 64, 64 at d = 128: 32000 and 64000, both
+    below fp16's 65504). The partial here spans 128 keys but carries p * 2^-s with the same bound;
+    unscaled it would be 128000 = inf in fp16."""
+    n = 1024
+    q = torch.zeros(1, 2, n, d, dtype=torch.float16, device=DEV)
+    k = torch.randn(1, 2, n, d, generator=torch.Generator().manual_seed(3)).half().to(DEV)
+    v = torch.full((1, 2, n, d), 1000.0, dtype=torch.float16, device=DEV)
+    for causal in (False, True):
+        out = fa.forward(q, k, v, causal=causal, fp16_accum=True)
+        assert torch.isfinite(out).all()
+        torch.testing.assert_close(out.float(), torch.full_like(out, 1000.0, dtype=torch.float32), atol=0.5, rtol=0)
+
+
 def test_fp16_accum_flag_selects_variant():
     _, _, _, qd, kd, vd = _qkv(1, 2, 256, 64, seed=8)
     assert torch.equal(fa.forward(qd, kd, vd, fp16_accum=True), fa.forward_variant(qd, kd, vd, variant="fp16acc"))
