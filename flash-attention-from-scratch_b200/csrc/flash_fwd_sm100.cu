@@ -135,7 +135,9 @@ struct FwdCfg {
     // Shared memory (offsets from a 1024-byte aligned base).
     static constexpr int kSmemQ = 0;
     static constexpr int kSmemKV = NQ * kTileBytes;
-    static constexpr int kSmemBytes = kSmemKV + STAGES * kTileBytes;
+    // O staging tile of the persistent grid's epilogue (the Q buffers hold the next item's Q).
+    static constexpr int kSmemStage = kSmemKV + STAGES * kTileBytes;
+    static constexpr int kSmemBytes = kSmemStage + kTileBytes;
     static constexpr int kSmemAlloc = kSmemBytes + 1024;
     // Tensor memory columns.
     static constexpr int kTmemS = 0;
@@ -186,6 +188,7 @@ struct SharedBarriers {
     uint64_t o_done[2];
     uint64_t q_empty[2];
     uint64_t epi[2];
+    uint64_t stg_free;  // persistent grid: the staging tile's turns, tile 0 then tile 1 per item
     uint64_t mma_idle;
     uint32_t tmem_base;
     int abort;
@@ -365,6 +368,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             mbar_init(smem_u32(&sb.kv_empty[s]), Cfg::kIssuers);
         }
         mbar_init(smem_u32(&sb.mma_idle), Cfg::kIssuers);
+        mbar_init(smem_u32(&sb.stg_free), 1);
         mbar_fence_init();
     }
     if (warp == Cfg::kMmaWarp) {
@@ -436,6 +440,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         };
 
         int g0 = 0;  // S / P / P.V count of this tile before the current item
+        int stg_items = 0;  // persistent grid: items whose epilogue took a staging turn
         bool ok = true;
 
         // A warp that gave up on a wait keeps walking its items and key tiles without touching
@@ -739,29 +744,62 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     }
                 }
                 __syncwarp();
-            } else if (ok && nt > 0) {
-                // O row (this thread's D columns), normalised, as fp16 straight to global
-                // memory: 16-byte stores, rows >= N skipped.
-                const float inv_sum = (row_sum > 0.0f) ? (1.0f / row_sum) : 0.0f;
-                uint4* dst = reinterpret_cast<uint4*>(args.o) +
-                             ((static_cast<size_t>(it.bh) * n + grow) * D) / 8;
+            } else if (!tma_store_o) {
+                // Persistent grid (the Q buffers already hold the next item's Q): O goes through
+                // the staging tile, which the query tiles take in turns, tile 0 then tile 1 of
+                // each item; the turn passes once the TMA store has read the tile. A tile with
+                // nothing to store still takes and passes its turn.
+                const int use = NQ * stg_items + t;
+                bool turn = ok;
+                if (turn && use > 0) {
+                    turn = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sb.stg_free), (use - 1) & 1, wctx,
+                                                             kStatusTimeoutEpilogue));
+                }
+                uint8_t* out = smem + Cfg::kSmemStage;
+                if (turn && nt > 0) {
+                    const float inv_sum = (row_sum > 0.0f) ? (1.0f / row_sum) : 0.0f;
 #pragma unroll
-                for (int c = 0; c < D / 32; ++c) {
-                    uint32_t o[32];
-                    tmem_ld32(t_o + c * 32, o);
-                    tmem_wait_ld();
-                    if (grow < n) {
+                    for (int c = 0; c < D / 32; ++c) {
+                        uint32_t o[32];
+                        tmem_ld32(t_o + c * 32, o);
+                        tmem_wait_ld();
+                        uint32_t h[16];
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) {
+                            h[e] = pack_half2(u2f(o[2 * e]) * inv_sum, u2f(o[2 * e + 1]) * inv_sum);
+                        }
+                        const int col = c * 32;
+                        const int box = col / 64;
+                        const int chunk0 = (col % 64) / 8;
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
-                            const uint4 v = make_uint4(
-                                pack_half2(u2f(o[8 * i + 0]) * inv_sum, u2f(o[8 * i + 1]) * inv_sum),
-                                pack_half2(u2f(o[8 * i + 2]) * inv_sum, u2f(o[8 * i + 3]) * inv_sum),
-                                pack_half2(u2f(o[8 * i + 4]) * inv_sum, u2f(o[8 * i + 5]) * inv_sum),
-                                pack_half2(u2f(o[8 * i + 6]) * inv_sum, u2f(o[8 * i + 7]) * inv_sum));
-                            dst[c * 4 + i] = v;
+                            const int cc = chunk0 + i;
+                            uint4* dst = reinterpret_cast<uint4*>(out + box * kBoxBytes + row * 128 +
+                                                                  ((cc ^ (row & 7)) << 4));
+                            *dst = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
                         }
                     }
+                    fence_proxy_async_smem();
                 }
+                __syncwarp();
+                if (ok && lane == 0) {
+                    mbar_arrive(smem_u32(&sb.epi[t]));
+                }
+                if (ok && row == 0) {
+                    // The store clips rows >= N (the tensor map's bound).
+                    if (mbar_wait(smem_u32(&sb.epi[t]), stg_items & 1, wctx, kStatusTimeoutEpilogue) && turn &&
+                        nt > 0) {
+#pragma unroll
+                        for (int b = 0; b < Cfg::kBoxes; ++b) {
+                            tma_store_3d(&tm_o, smem_u32(out) + b * kBoxBytes, b * 64, q0, it.bh);
+                        }
+                        tma_store_commit();
+                        tma_store_wait_read();
+                    }
+                    mbar_arrive(smem_u32(&sb.stg_free));
+                }
+                __syncwarp();
+                ++stg_items;
             }
             g0 += nt;
         }
