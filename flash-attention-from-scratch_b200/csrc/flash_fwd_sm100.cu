@@ -10,12 +10,13 @@
 // on diagonal / ragged tiles, lazy rescaling for the "opt" variant, per-tile fp16 partials for
 // "fp16acc") is the reference's, the machine mapping is new:
 //
-// Work item = one (b,h) head x NQ consecutive 128-row query tiles (NQ = 2, or 1 for fp16acc)
+// Work item = one (b,h) head x NQ consecutive 128-row query tiles (NQ = 2; 1 for fp16acc, d = 128)
 // x one key range (split-KV). Each CTA runs one item, or, for short rows (N <= 2048), a
 // persistent grid of one CTA per SM walks the items: every role loops over the same items
 // and the barrier phases run on across them, so an item's Q load and first S overlap the
-// previous item's last tiles and epilogue. O leaves through the Q buffer and a TMA store (one
-// item per CTA) or as direct 16-byte row stores (persistent).
+// previous item's last tiles and epilogue. O leaves through a TMA store, staged in the tile's
+// Q buffer (one item per CTA) or in a staging tile after the K/V ring that the query tiles
+// take in turns (persistent grid).
 // Warp roles (warp-specialised, one CTA per SM, whole warpgroups):
 //   warpgroup t < NQ    softmax for query tile t; thread i of the warpgroup owns TMEM lane i
 //                       = query row i of the tile, so row max and row sum need no shuffles.
@@ -31,14 +32,15 @@
 //   between the softmax warpgroups and the producer/MMA warpgroup (setmaxnreg).
 //
 // Tensor memory (512 columns x 128 lanes, fp32 cells):
-//   S_t  columns [128 t, 128 t + 128)   scores of tile t, fp32
-//   O_t  columns [128 NQ + D t, +D)     fp32 output accumulator of tile t
+//   S_t  columns [128 t, 128 t + 128)   scores of tile t, fp32 (fp16acc at d = 128, NQ = 1: two
+//        S buffers, columns [0, 128) and [128, 256), for alternate key tiles)
+//   O_t  columns [128 NQ kSBufs + D t, +D)  fp32 output accumulator of tile t
 //   P_t  (d = 128) columns [128 t, +64) over S_t once S_t has been read: S_t(j+1) is issued
 //        after PV_t(j), and tcgen05.mma operations of one thread execute in issue order;
 //        (d = 64) its own columns [128 NQ + D NQ + 64 t, +64), so that S_t(j+1) can run while
 //        the softmax of tile j is still computing P_t(j).
-//   T_t  (fp16acc) columns [128 NQ + D NQ + D t, +D): fp16 partial of P.V over the current
-//        K/V tile, one value per column; P_t lies over S_t as at d = 128.
+//   T_t  (fp16acc) the D columns after the O_t: fp16 partial of P.V over the current K/V tile,
+//        one value per column; P_t lies over S_t as at d = 128.
 
 #include <cuda.h>
 #include <cuda_fp16.h>
