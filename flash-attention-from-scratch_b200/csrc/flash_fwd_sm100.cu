@@ -104,6 +104,7 @@ constexpr int kBM = 128;             // query rows per tile (= TMEM lanes = MMA 
 constexpr int kBN = 128;             // keys per K/V tile (= MMA N of Q K^T)
 constexpr int kBoxBytes = 128 * 128; // one TMA box: 128 rows x 64 fp16 (128 B, one swizzle span)
 constexpr int kPersistentMaxN = 2048; // persistent grid (one CTA per SM walks the items) up to this N
+constexpr int kPersistentMaxNFull = 8192;  // ... and up to this N without the causal mask
 
 template <int D_, bool CAUSAL_, int VARIANT_>
 struct FwdCfg {
@@ -1411,8 +1412,10 @@ Plan make_plan(int num_bh, int seqlen, int head_dim, bool causal, int variant, i
     const int key_tiles = (seqlen + kBN - 1) / kBN;
     // Short rows run on a persistent grid, so that each item's Q load and first S overlap the
     // previous item's tail (measured: B16 H16 N1000 d128 causal 496 -> 554 TFLOPS); longer rows
-    // one CTA per item (cfg1 N4096: 911 vs 862 persistent).
-    p.persistent = seqlen <= kPersistentMaxN;
+    // one CTA per item (cfg1 N4096 causal: 911 vs 862 persistent, its items differ in length).
+    // Without the mask every item costs the same and the static assignment stays balanced: N3000
+    // d128 937 -> 983, d64 581 -> 631, N4096 d128 963 -> 1001; N8192 and 16384 unchanged.
+    p.persistent = seqlen <= kPersistentMaxN || (!causal && seqlen <= kPersistentMaxNFull);
     // Split-KV when the row blocks leave SMs idle (few heads x long rows): about SMs / row
     // blocks ranges, at least two key tiles each, at most 16.
     int splits = num_splits;

@@ -57,6 +57,15 @@ def test_fp16acc_d128_one_query_tile_per_item():
     assert plan(1, 4, 4096, 64, False, "fp16acc")["rows_per_item"] == 256
 
 
+@pytest.mark.parametrize("n", [3000, 4096, 8192])
+def test_noncausal_rows_up_to_8192_persistent_grid(n):
+    # equal-cost items: the static assignment of a persistent grid stays balanced
+    pl = plan(16, 16, n, 128, False)
+    assert pl["persistent"] == 1 and pl["ctas"] == 148
+    assert plan(16, 16, n, 128, True)["persistent"] == (1 if n <= 2048 else 0)
+    assert plan(16, 16, 8193, 128, False)["persistent"] == 0
+
+
 def test_tail_split_needs_eight_key_tiles_per_piece():
     # N = 1024: 8 key tiles, a piece of half would hold 4: no tail split
     assert plan(1, 80, 1024, 128, False)["tail_blocks"] == 0
