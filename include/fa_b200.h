@@ -121,8 +121,8 @@ FA_API int fa_flash_fwd_splitkv(const FaFwdParams* params, int32_t num_splits, v
 typedef struct FaPlan {
     int32_t rows_per_item;  /* query rows per work item: 128 x query tiles per CTA (256, or 128
                                for fp16acc at head_dim 128) */
-    int32_t persistent;     /* 1: a grid of one CTA per SM walks the items (short rows);
-                               0: one CTA per item */
+    int32_t persistent;     /* 1: a grid of one CTA per SM walks the items (rows up to 2048,
+                               non-causal rows up to 8192); 0: one CTA per item */
     int32_t num_splits;     /* key ranges of every row block (split-KV); 1 = none */
     int32_t tail_blocks;    /* non-causal: row blocks of the grid's last partial wave, each cut
                                into tail_splits key ranges; 0 = none */
