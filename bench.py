@@ -15,8 +15,9 @@ process per GPU, no collective on the data path: strong scaling. A step is one f
 over the whole problem (every rank's shard); value = the problem's FLOPs / the max over ranks
 of the event-timed duration. The same line carries the non-causal twin (cfg3nc) on the same
 shards, at N > 1 the weak-scaling figure (every rank a private copy of config 1), and at N = 1
-`per_config`: configs 1 and 2 (fp32 and fp16 accumulation) and rows of the ragged sweep
-(config 4), each event-timed for K steps with its clocks.
+`per_config`: configs 1 and 2 (fp32 and fp16 accumulation), configs 3 (causal) and 2 with
+bfloat16 inputs, and rows of the ragged sweep (config 4), each event-timed for K steps with its
+clocks.
 
 `value` is timed on the device with CUDA events around exactly K steps with inputs resident in
 HBM (inputs larger than L2); `e2e` is the same metric through the public API with host
@@ -58,7 +59,7 @@ PKG = REPO / "flash-attention-from-scratch_b200"
 
 METRIC = "attn fwd TFLOPS (fp16, d=64/128, causal+non) at 1/2/4/8 B200; % of TC peak"
 HEADLINE = "cfg3"
-PER_CONFIG = ["cfg1", "cfg2", "cfg2acc", "cfg4:8191:128:1", "cfg4:12345:128:0", "cfg4:12345:64:1",
+PER_CONFIG = ["cfg1", "cfg2", "cfg2acc", "cfg3bf16", "cfg2bf16", "cfg4:8191:128:1", "cfg4:12345:128:0", "cfg4:12345:64:1",
               "cfg4:3000:128:0", "cfg4:1000:128:1", "cfg4:1000:64:0"]
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
@@ -95,6 +96,9 @@ def workload(name: str) -> dict:
         return dict(syn.CONFIGS[name], outliers=False, variant="opt", name=name)
     if name == "cfg2acc":
         return dict(syn.CONFIGS["cfg2"], outliers=False, variant="fp16acc", name=name)
+    if name.endswith("bf16") and name[: -len("bf16")] in syn.CONFIGS:
+        # a configuration's shape and values with bfloat16 inputs (an extension of the reference)
+        return dict(syn.CONFIGS[name[: -len("bf16")]], outliers=False, variant="opt", dtype="bf16", name=name)
     if name.startswith("cfg4:"):
         # cfg4:N:d:causal, e.g. cfg4:12345:128:1 (B16 H16, seed 4, outlier channel)
         _, n, d, causal = name.split(":")
@@ -666,7 +670,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                 oc = syn.outlier_channels(pc["d"])
                 pq[..., :oc] *= 8.0
                 pk[..., :oc] *= 8.0
-            pq, pk, pv = pq.half(), pk.half(), pv.half()
+            pdt = torch.bfloat16 if pc.get("dtype") == "bf16" else torch.float16
+            pq, pk, pv = pq.to(pdt), pk.to(pdt), pv.to(pdt)
 
             def pc_step():
                 return _C.forward(pq, pk, pv, pc["causal"], None, pc["variant"])
@@ -677,7 +682,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             io = 4 * pq.numel() * 2
             per_config[name] = {
                 "B": pc["b"], "H": pc["h"], "N": pc["n"], "d": pc["d"], "causal": pc["causal"],
-                "variant": pc["variant"], "outliers": bool(pc.get("outliers")), "value": p_val, "unit": "TFLOPS",
+                "variant": pc["variant"], "dtype": pc.get("dtype", "f16"), "outliers": bool(pc.get("outliers")),
+                "value": p_val, "unit": "TFLOPS",
                 "ms_per_step": p_ms, "frac": p_val / peak, "hbm_gbs_algorithmic": io / (p_ms * 1e-3) / 1e9,
                 "kernels_per_launch": kernels_per_launch(pq, pk, pv, pc["causal"], pc["variant"]),
                 "plan": plan_of(pq, pc["causal"], pc["variant"]),

@@ -93,6 +93,14 @@ int validate(const FaFwdParams* p) {
     if (p->variant > FA_VARIANT_FP16ACC) {
         return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd: unknown variant");
     }
+    if (p->dtype > FA_DTYPE_BFLOAT16) {
+        return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd: dtype must be FA_DTYPE_FLOAT16 or FA_DTYPE_BFLOAT16");
+    }
+    if (p->dtype == FA_DTYPE_BFLOAT16 && p->variant == FA_VARIANT_FP16ACC) {
+        // kind::f16 MMAs accumulate bfloat16 products in fp32 only; the fp16 partials of
+        // fp16acc need float16 operands.
+        return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd: the fp16acc variant needs float16 inputs");
+    }
     if (p->q == nullptr || p->k == nullptr || p->v == nullptr || p->o == nullptr) {
         return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd: null tensor pointer");
     }
@@ -145,6 +153,7 @@ int launch_one(const FaFwdParams* p, cudaStream_t stream, int num_splits, void* 
     prob.head_dim = p->head_dim;
     prob.causal = p->causal != 0;
     prob.variant = p->variant;
+    prob.bf16 = p->dtype == FA_DTYPE_BFLOAT16;
     fa_sm100::FwdArgs args{};
     args.seqlen = p->seqlen;
     args.num_bh = bh;

@@ -72,7 +72,7 @@ struct FwdArgs {
     float* ws_o;          // split records x D fp32 (see splitkv records in the kernel)
     float* ws_ml;         // split records x 2 fp32: m (log2 units), l
     int num_items;        // work items, set by the launcher
-    void* o;              // output [num_bh][seqlen][D] fp16, set by the launcher
+    void* o;              // output [num_bh][seqlen][D] fp16 / bf16, set by the launcher
 };
 
 // Split-KV workspace bytes for a problem (16-byte aligned sections).
@@ -112,7 +112,8 @@ int device_sm_count();
 // Variant ids as in the reference (csrc/flash_fwd.h:12-16).
 enum : int { kVariantBaseline = 0, kVariantOpt = 1, kVariantFp16Acc = 2 };
 
-// One forward problem: q, k, v, o are contiguous [B*H][N][D] fp16 device tensors.
+// One forward problem: q, k, v, o are contiguous [B*H][N][D] fp16 (bf16: bfloat16) device
+// tensors.
 struct FwdProblem {
     const void* q;
     const void* k;
@@ -123,6 +124,7 @@ struct FwdProblem {
     int head_dim;
     bool causal;
     int variant;
+    bool bf16;
 };
 
 // Unique id (cuCtxGetId, plus one) of the calling thread's current CUDA context, or 0 when
@@ -185,7 +187,7 @@ inline cudaError_t ensure_smem_limit(int bytes) {
 
 // Launches the split-KV combine over the rows of every split row block (all of them with
 // num_splits > 1, the tail blocks with a tail split):
-// O[bh][row] = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s, fp16.
+// O[bh][row] = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s, in the problem's element type.
 cudaError_t launch_splitkv_combine(const FwdProblem& prob, const FwdArgs& args, const Plan& plan,
                                    cudaStream_t stream);
 

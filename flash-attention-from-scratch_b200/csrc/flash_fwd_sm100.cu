@@ -2,7 +2,7 @@
 // memory, online base-2 softmax in warpgroups that own one TMEM lane (= one query row) per
 // thread, TMA epilogue.
 //
-//   O = softmax(Q K^T * scale) V        Q, K, V, O: [B, H, N, D] fp16, D in {64, 128}
+//   O = softmax(Q K^T * scale) V        Q, K, V, O: [B, H, N, D] fp16 (or bf16), D in {64, 128}
 //
 // It replaces the reference's mma.sync kernel (csrc/kernels/flash_fwd.cu:154-561) and its
 // launcher (:563-652) behind the same parameters; the algorithm (FA2 online softmax with the
@@ -106,11 +106,16 @@ constexpr int kBoxBytes = 128 * 128; // one TMA box: 128 rows x 64 fp16 (128 B, 
 constexpr int kPersistentMaxN = 2048; // persistent grid (one CTA per SM walks the items) up to this N
 constexpr int kPersistentMaxNFull = 8192;  // ... and up to this N without the causal mask
 
-template <int D_, bool CAUSAL_, int VARIANT_>
+template <int D_, bool CAUSAL_, int VARIANT_, bool BF16_ = false>
 struct FwdCfg {
     static constexpr int D = D_;
     static constexpr bool CAUSAL = CAUSAL_;
     static constexpr int VARIANT = VARIANT_;
+    // Element type of Q, K, V, O and of P (the P.V operand): bfloat16 when BF16, else float16.
+    // The MMAs accumulate in fp32 either way; bf16 operands have no fp16 accumulator, so the
+    // fp16acc variant is float16 only.
+    static constexpr bool BF16 = BF16_;
+    static_assert(!(BF16_ && VARIANT_ == kVariantFp16Acc), "fp16acc needs float16 operands");
     // fp16acc (reference ACC16, flash_fwd.cu:439-470): P.V of each 128-key tile accumulated in
     // fp16 into a fresh partial T_t, which the softmax folds into the fp32 O_t. Exact max (no
     // lazy rescale), so p <= 1. P is stored as p * 2^-kAccShift, which bounds |T_t| by
@@ -209,7 +214,7 @@ __device__ __forceinline__ float f16cell_to_float(uint32_t cell) {
 // tile's first byte.
 template <class Cfg>
 __device__ __forceinline__ void issue_s_mma(uint32_t tmem_s, uint64_t qd, uint64_t kd) {
-    constexpr uint32_t idesc = make_idesc_f16(kBM, kBN, /*d_f32=*/true, /*b_mn_major=*/false);
+    constexpr uint32_t idesc = make_idesc_f16(kBM, kBN, /*d_f32=*/true, /*b_mn_major=*/false, Cfg::BF16);
 #pragma unroll
     for (int kk = 0; kk < Cfg::D / 16; ++kk) {
         const uint64_t off = static_cast<uint64_t>(((kk / 4) * kBoxBytes + (kk % 4) * 32) >> 4);
@@ -221,7 +226,7 @@ __device__ __forceinline__ void issue_s_mma(uint32_t tmem_s, uint64_t qd, uint64
 template <class Cfg>
 __device__ __forceinline__ void issue_pv_mma_f32(uint32_t tmem_o, uint32_t tmem_p, uint64_t vd,
                                                  bool first) {
-    constexpr uint32_t idesc = make_idesc_f16(kBM, Cfg::D, /*d_f32=*/true, /*b_mn_major=*/true);
+    constexpr uint32_t idesc = make_idesc_f16(kBM, Cfg::D, /*d_f32=*/true, /*b_mn_major=*/true, Cfg::BF16);
 #pragma unroll
     for (int kk = 0; kk < kBN / 16; ++kk) {
         umma_ts(tmem_o, tmem_p + kk * 8, vd + static_cast<uint64_t>(kk * (2048 >> 4)), idesc,
@@ -562,13 +567,13 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                         const float2 e = ((i % 8) < Cfg::kEmuPer8)
                                              ? (Cfg::kPolyDeg == 3 ? exp2_poly2_deg3(x2) : exp2_poly2(x2))
                                              : make_float2(ex2_approx(x2.x), ex2_approx(x2.y));
-                        const uint32_t h = pack_half2(e.x, e.y);
+                        const uint32_t h = pack2<Cfg::BF16>(e.x, e.y);
                         // The row sum adds the fp16-rounded values the MMA consumes, so that O
                         // is normalised by the weights it was accumulated with. (The reference
                         // sums the fp32 values, csrc/kernels/flash_fwd.cu:403-417; measured here
                         // that adds error: cfg4's outlier rows exceed 2e-3.)
                         // fp32 += fp16 with the mixed-precision add (no separate conversion).
-                        add_f16x2_to_f32(sum2[i % 4].x, sum2[i % 4].y, h);
+                        add_x2_to_f32<Cfg::BF16>(sum2[i % 4].x, sum2[i % 4].y, h);
                         pk[i] = h;
                     }
                     if (kLateWait && chunk == 0 && j > 0) {
@@ -718,7 +723,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     uint32_t h[16];
 #pragma unroll
                     for (int e = 0; e < 16; ++e) {
-                        h[e] = pack_half2(u2f(o[2 * e]) * inv_sum, u2f(o[2 * e + 1]) * inv_sum);
+                        h[e] = pack2<Cfg::BF16>(u2f(o[2 * e]) * inv_sum, u2f(o[2 * e + 1]) * inv_sum);
                     }
                     const int col = c * 32;  // first O column of this chunk
                     const int box = col / 64;
@@ -769,7 +774,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                         uint32_t h[16];
 #pragma unroll
                         for (int e = 0; e < 16; ++e) {
-                            h[e] = pack_half2(u2f(o[2 * e]) * inv_sum, u2f(o[2 * e + 1]) * inv_sum);
+                            h[e] = pack2<Cfg::BF16>(u2f(o[2 * e]) * inv_sum, u2f(o[2 * e + 1]) * inv_sum);
                         }
                         const int col = c * 32;
                         const int box = col / 64;
@@ -1284,7 +1289,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 // Split-KV combine (reference: none; Flash-Decoding's merge of per-range softmax partials).
 // One warp per output row, lanes over the head dim, ranges merged in index order (so the result
 // is deterministic): M = max m_s over the ranges with l_s > 0, then
-// O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s, rounded to fp16.
+// O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s, rounded to fp16 (BF16: bfloat16).
 // Rows: with split-KV (tail_blocks == 0) every row of every head, row r of head bh at record
 // bh * rows_pad + r; with a tail split the rows of the tail blocks, row r of tail block p at
 // record p * rows_per_block + r, the block being row block tail_from + p of the non-causal item
@@ -1292,7 +1297,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 struct CombineArgs {
     const float* ws_o;
     const float2* ws_ml;
-    __half* o;
+    void* o;                 // [B*H][N][D] fp16 or bf16
     int n;
     int num_splits;
     long long split_stride;  // records per key range
@@ -1304,7 +1309,7 @@ struct CombineArgs {
     int rows_pad;
 };
 
-template <int D>
+template <int D, bool BF16>
 __global__ void __launch_bounds__(256) splitkv_combine_kernel(const CombineArgs a) {
     constexpr int PER = D / 32;  // columns per lane
     const long long item = static_cast<long long>(blockIdx.x) * 8 + threadIdx.x / 32;
@@ -1363,12 +1368,12 @@ __global__ void __launch_bounds__(256) splitkv_combine_kernel(const CombineArgs 
         }
     }
     const float inv = (l > 0.0f) ? (1.0f / l) : 0.0f;
-    __half* dst = a.o + out_row * D + lane * PER;
+    uint16_t* dst = static_cast<uint16_t*>(a.o) + out_row * D + lane * PER;
     if constexpr (PER == 4) {
         *reinterpret_cast<uint2*>(dst) =
-            make_uint2(pack_half2(acc[0] * inv, acc[1] * inv), pack_half2(acc[2] * inv, acc[3] * inv));
+            make_uint2(pack2<BF16>(acc[0] * inv, acc[1] * inv), pack2<BF16>(acc[2] * inv, acc[3] * inv));
     } else {
-        *reinterpret_cast<uint32_t*>(dst) = pack_half2(acc[0] * inv, acc[1] * inv);
+        *reinterpret_cast<uint32_t*>(dst) = pack2<BF16>(acc[0] * inv, acc[1] * inv);
     }
 }
 
@@ -1485,10 +1490,10 @@ Plan make_plan(int num_bh, int seqlen, int head_dim, bool causal, int variant, i
     return p;
 }
 
-template <int D, bool CAUSAL, int VARIANT>
+template <int D, bool CAUSAL, int VARIANT, bool BF16 = false>
 cudaError_t launch_cfg(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                        const CUtensorMap& tm_o, const FwdArgs& args, const Plan& plan, cudaStream_t stream) {
-    using Cfg = FwdCfg<D, CAUSAL, VARIANT>;
+    using Cfg = FwdCfg<D, CAUSAL, VARIANT, BF16>;
     auto* kernel = fa_fwd_sm100_kernel<Cfg>;
     cudaError_t err = ensure_smem_limit<fa_fwd_sm100_kernel<Cfg>>(Cfg::kSmemAlloc);
     if (err != cudaSuccess) {
@@ -1503,9 +1508,20 @@ cudaError_t launch_cfg(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const C
 }
 
 template <int D, bool CAUSAL>
-cudaError_t launch_variant(int variant, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+cudaError_t launch_variant(int variant, bool bf16, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                            const CUtensorMap& tm_v, const CUtensorMap& tm_o, const FwdArgs& args,
                            const Plan& plan, cudaStream_t stream) {
+    if (bf16) {
+        // bfloat16 inputs: the fp32-accumulating variants only (validated by the C ABI).
+        switch (variant) {
+            case kVariantBaseline:
+                return launch_cfg<D, CAUSAL, kVariantBaseline, true>(tm_q, tm_k, tm_v, tm_o, args, plan, stream);
+            case kVariantOpt:
+                return launch_cfg<D, CAUSAL, kVariantOpt, true>(tm_q, tm_k, tm_v, tm_o, args, plan, stream);
+            default:
+                return cudaErrorInvalidValue;
+        }
+    }
     switch (variant) {
         case kVariantBaseline:
             return launch_cfg<D, CAUSAL, kVariantBaseline>(tm_q, tm_k, tm_v, tm_o, args, plan, stream);
@@ -1524,7 +1540,7 @@ cudaError_t launch_forward(const FwdProblem& prob, const FwdArgs& args, const Pl
     CUtensorMap maps[4];
     const void* ptrs[4] = {prob.q, prob.k, prob.v, prob.o};
     for (int i = 0; i < 4; ++i) {
-        if (encode_bhnd_map(&maps[i], ptrs[i], prob.num_bh, prob.seqlen, prob.head_dim, kBM) !=
+        if (encode_bhnd_map(&maps[i], ptrs[i], prob.num_bh, prob.seqlen, prob.head_dim, kBM, prob.bf16) !=
             CUDA_SUCCESS) {
             return cudaErrorInvalidValue;
         }
@@ -1546,15 +1562,16 @@ cudaError_t launch_forward(const FwdProblem& prob, const FwdArgs& args, const Pl
     a.div_tail = FastDiv(a.tail_splits);
     a.tail_from = plan.tail_blocks > 0 ? plan.row_blocks - plan.tail_blocks : plan.items;
     const int variant = prob.variant;
+    const bool bf16 = prob.bf16;
     if (prob.head_dim == 64) {
         return prob.causal
-                   ? launch_variant<64, true>(variant, maps[0], maps[1], maps[2], maps[3], a, plan, stream)
-                   : launch_variant<64, false>(variant, maps[0], maps[1], maps[2], maps[3], a, plan, stream);
+                   ? launch_variant<64, true>(variant, bf16, maps[0], maps[1], maps[2], maps[3], a, plan, stream)
+                   : launch_variant<64, false>(variant, bf16, maps[0], maps[1], maps[2], maps[3], a, plan, stream);
     }
     if (prob.head_dim == 128) {
         return prob.causal
-                   ? launch_variant<128, true>(variant, maps[0], maps[1], maps[2], maps[3], a, plan, stream)
-                   : launch_variant<128, false>(variant, maps[0], maps[1], maps[2], maps[3], a, plan, stream);
+                   ? launch_variant<128, true>(variant, bf16, maps[0], maps[1], maps[2], maps[3], a, plan, stream)
+                   : launch_variant<128, false>(variant, bf16, maps[0], maps[1], maps[2], maps[3], a, plan, stream);
     }
     return cudaErrorInvalidValue;
 }
@@ -1588,7 +1605,7 @@ cudaError_t launch_splitkv_combine(const FwdProblem& prob, const FwdArgs& args, 
     CombineArgs a{};
     a.ws_o = args.ws_o;
     a.ws_ml = reinterpret_cast<const float2*>(args.ws_ml);
-    a.o = static_cast<__half*>(prob.o);
+    a.o = prob.o;
     a.n = prob.seqlen;
     a.nb = (prob.seqlen + plan.rows_per_item - 1) / plan.rows_per_item;
     a.rows_per_block = plan.rows_per_item;
@@ -1606,9 +1623,17 @@ cudaError_t launch_splitkv_combine(const FwdProblem& prob, const FwdArgs& args, 
     }
     const dim3 grid(static_cast<unsigned>((a.rows + 7) / 8));
     if (prob.head_dim == 64) {
-        splitkv_combine_kernel<64><<<grid, 256, 0, stream>>>(a);
+        if (prob.bf16) {
+            splitkv_combine_kernel<64, true><<<grid, 256, 0, stream>>>(a);
+        } else {
+            splitkv_combine_kernel<64, false><<<grid, 256, 0, stream>>>(a);
+        }
     } else {
-        splitkv_combine_kernel<128><<<grid, 256, 0, stream>>>(a);
+        if (prob.bf16) {
+            splitkv_combine_kernel<128, true><<<grid, 256, 0, stream>>>(a);
+        } else {
+            splitkv_combine_kernel<128, false><<<grid, 256, 0, stream>>>(a);
+        }
     }
     return cudaGetLastError();
 }

@@ -316,10 +316,14 @@ __host__ __device__ constexpr uint64_t make_desc_mnmajor_sw128(uint32_t saddr,
 }
 
 // Instruction descriptor for kind::f16 (32 bit):
-//   [4,6) D format (0 = f16, 1 = f32)   [7,10) A format (0 = f16)   [10,13) B format (0 = f16)
-//   [15] A major (0 = K)   [16] B major (0 = K, 1 = MN)   [17,23) N >> 3   [24,29) M >> 4
-__host__ __device__ constexpr uint32_t make_idesc_f16(int m, int n, bool d_f32, bool b_mn_major) {
+//   [4,6) D format (0 = f16, 1 = f32)   [7,10) A format (0 = f16, 1 = bf16)
+//   [10,13) B format (0 = f16, 1 = bf16)   [15] A major (0 = K)   [16] B major (0 = K, 1 = MN)
+//   [17,23) N >> 3   [24,29) M >> 4
+// A and B always get the same format (bf16 operands accumulate into an f32 D only).
+__host__ __device__ constexpr uint32_t make_idesc_f16(int m, int n, bool d_f32, bool b_mn_major,
+                                                      bool ab_bf16 = false) {
     return (static_cast<uint32_t>(d_f32 ? 1 : 0) << 4) |
+           (static_cast<uint32_t>(ab_bf16 ? 1 : 0) << 7) | (static_cast<uint32_t>(ab_bf16 ? 1 : 0) << 10) |
            (static_cast<uint32_t>(b_mn_major ? 1 : 0) << 16) |
            (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
@@ -400,6 +404,40 @@ __device__ __forceinline__ void add_f16x2_to_f32(float& lo_acc, float& hi_acc, u
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     const __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// bfloat16 counterparts: lo_acc += low half of b, hi_acc += high half (bf16 -> fp32 exactly,
+// then an fp32 add), and two floats rounded to nearest-even bfloat16, lo in the low half.
+__device__ __forceinline__ void add_bf16x2_to_f32(float& lo_acc, float& hi_acc, uint32_t b) {
+    asm("{\n\t.reg .b16 l, u;\n\tmov.b32 {l, u}, %2;\n\t"
+        "add.rn.f32.bf16 %0, l, %0;\n\tadd.rn.f32.bf16 %1, u, %1;\n\t}"
+        : "+f"(lo_acc), "+f"(hi_acc)
+        : "r"(b));
+}
+
+__device__ __forceinline__ uint32_t pack_bf162(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+// The element type's pair helpers, chosen at compile time (BF16: bfloat16, else float16).
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    if constexpr (BF16) {
+        return pack_bf162(lo, hi);
+    } else {
+        return pack_half2(lo, hi);
+    }
+}
+
+template <bool BF16>
+__device__ __forceinline__ void add_x2_to_f32(float& lo_acc, float& hi_acc, uint32_t h) {
+    if constexpr (BF16) {
+        add_bf16x2_to_f32(lo_acc, hi_acc, h);
+    } else {
+        add_f16x2_to_f32(lo_acc, hi_acc, h);
+    }
 }
 
 __device__ __forceinline__ float2 unpack_half2(uint32_t r) {

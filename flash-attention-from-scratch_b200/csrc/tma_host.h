@@ -1,5 +1,5 @@
 #pragma once
-// Host-side TMA tensor-map encoding for [heads][rows][head_dim] fp16 tensors.
+// Host-side TMA tensor-map encoding for [heads][rows][head_dim] fp16 / bf16 tensors.
 // cuTensorMapEncodeTiled is fetched through the runtime's driver entry point, so the library
 // does not link libcuda directly.
 
@@ -27,11 +27,12 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// 3-D map over a contiguous [heads][rows][head_dim] fp16 tensor: dims (innermost first)
-// {head_dim, rows, heads}, box {64, box_rows, 1}, 128-byte swizzle, zero fill out of bounds.
-// Out-of-range rows of a head are zero-filled on load and dropped on store, per head.
+// 3-D map over a contiguous [heads][rows][head_dim] fp16 (bf16: bfloat16) tensor: dims
+// (innermost first) {head_dim, rows, heads}, box {64, box_rows, 1}, 128-byte swizzle, zero fill
+// out of bounds. Out-of-range rows of a head are zero-filled on load and dropped on store, per
+// head.
 inline CUresult encode_bhnd_map(CUtensorMap* map, const void* base, int heads, int rows,
-                                int head_dim, int box_rows) {
+                                int head_dim, int box_rows, bool bf16 = false) {
     auto fn = tensor_map_encoder();
     if (fn == nullptr) {
         return CUDA_ERROR_NOT_SUPPORTED;
@@ -42,8 +43,9 @@ inline CUresult encode_bhnd_map(CUtensorMap* map, const void* base, int heads, i
                                    static_cast<cuuint64_t>(rows) * head_dim * 2};
     const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_rows), 1};
     const cuuint32_t elem_strides[3] = {1, 1, 1};
-    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box,
-              elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+    const CUtensorMapDataType type = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    return fn(map, type, 3, const_cast<void*>(base), dims, strides, box, elem_strides,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 

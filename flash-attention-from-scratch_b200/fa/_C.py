@@ -29,6 +29,10 @@ FA_ERR_DEVICE_TIMEOUT = 3
 
 VARIANTS = {"baseline": 0, "opt": 1, "fp16acc": 2}
 
+# FaFwdParams.dtype (FA_DTYPE_*): the element type of q, k, v and O. bfloat16 is an extension
+# of the reference, which takes float16 only (csrc/bindings.cpp:34).
+DTYPES = {torch.float16: 0, torch.bfloat16: 1}
+
 
 class FaFwdParams(ctypes.Structure):
     """ctypes image of ``FaFwdParams`` (include/fa_b200.h)."""
@@ -45,7 +49,8 @@ class FaFwdParams(ctypes.Structure):
         ("softmax_scale", ctypes.c_float),
         ("causal", ctypes.c_uint8),
         ("variant", ctypes.c_uint8),
-        ("reserved", ctypes.c_uint8 * 2),
+        ("dtype", ctypes.c_uint8),
+        ("reserved", ctypes.c_uint8),
     ]
 
 
@@ -126,12 +131,15 @@ def parse_variant(name: str) -> int:
 
 
 def check_inputs(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
-    """The TORCH_CHECKs of csrc/bindings.cpp:31-40, in the same order and wording."""
+    """The TORCH_CHECKs of csrc/bindings.cpp:31-40, in the same order and wording; the dtype
+    check also admits bfloat16 (all three tensors the same type), which the reference lacks."""
     for t in (q, k, v):
         if not t.is_cuda:
             raise RuntimeError("q, k, v must be CUDA tensors")
-        if t.dtype != torch.float16:
-            raise RuntimeError("q, k, v must be float16")
+        if t.dtype not in DTYPES:
+            raise RuntimeError("q, k, v must be float16 (or bfloat16)")
+        if t.dtype != q.dtype:
+            raise RuntimeError("q, k, v must have the same dtype")
         if not t.is_contiguous():
             raise RuntimeError("q, k, v must be contiguous")
         if t.dim() != 4:
@@ -149,6 +157,7 @@ def make_params(q, k, v, o, causal: bool, softmax_scale: float, variant: int) ->
     p.softmax_scale = float(softmax_scale)
     p.causal = 1 if causal else 0
     p.variant = variant
+    p.dtype = DTYPES[q.dtype]
     return p
 
 

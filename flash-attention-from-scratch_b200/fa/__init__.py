@@ -2,7 +2,8 @@
 
     import fa
     o = fa.forward(q, k, v, causal=False)      # q, k, v: [B, H, N, D] fp16 CUDA, D in {64, 128}
-    o = fa.forward(q, k, v, fp16_accum=True)   # P.V accumulated in fp16 per 64 keys
+    o = fa.forward(q, k, v, fp16_accum=True)   # P.V accumulated in fp16 per key tile
+    o = fa.forward(qb, kb, vb)                  # bfloat16 q, k, v (an extension): O in bf16
 
 Same public surface as the reference package (fa/__init__.py:14-38): ``forward``,
 ``forward_variant`` and ``attention_reference``; plus ``forward_splitkv``, ``forward_host`` (CPU
@@ -29,9 +30,12 @@ def forward(
 ) -> torch.Tensor:
     """O = softmax(Q K^T * scale) V.
 
-    fp16_accum: accumulate P @ V in fp16 within each 64-key half tile (folded into fp32
-    between them), the reference's "fp16acc" build. On B200 it runs no faster than fp32
-    accumulation; it exists for API and numerical parity.
+    fp16_accum: accumulate P @ V in fp16 within each 128-key tile (folded into fp32 between
+    tiles), the reference's "fp16acc" build. On B200 it runs no faster than fp32 accumulation;
+    it exists for API and numerical parity. float16 inputs only.
+
+    q, k, v may also be bfloat16 (all three; not in the reference): the same kernel with bf16
+    operands and fp32 accumulation, O returned in bf16.
     """
     variant = "fp16acc" if fp16_accum else "opt"
     return _C.forward(q, k, v, causal, softmax_scale, variant)

@@ -27,8 +27,10 @@ def _check_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
     for t in (q, k, v):
         if t.is_cuda:
             raise RuntimeError("forward_host: q, k, v must be CPU tensors (use fa.forward for CUDA tensors)")
-        if t.dtype != torch.float16:
-            raise RuntimeError("q, k, v must be float16")
+        if t.dtype not in (torch.float16, torch.bfloat16):
+            raise RuntimeError("q, k, v must be float16 (or bfloat16)")
+        if t.dtype != q.dtype:
+            raise RuntimeError("q, k, v must have the same dtype")
         if not t.is_contiguous():
             raise RuntimeError("q, k, v must be contiguous")
         if t.dim() != 4:

@@ -27,8 +27,10 @@ def make_qkv(
     scale: float = 1.0,
     outliers: bool = False,
     outlier_factor: float = 8.0,
+    dtype: torch.dtype = torch.float16,
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """CPU fp16 q, k, v of shape [b, h, n, d]."""
+    """CPU q, k, v of shape [b, h, n, d], rounded to `dtype` (fp16, or bf16 for the bfloat16
+    path) from the same fp32 draws."""
     g = torch.Generator().manual_seed(seed)
     q = torch.randn(b, h, n, d, generator=g) * scale
     k = torch.randn(b, h, n, d, generator=g) * scale
@@ -37,7 +39,7 @@ def make_qkv(
         c = outlier_channels(d)
         q[..., :c] *= outlier_factor
         k[..., :c] *= outlier_factor
-    return q.half(), k.half(), v.half()
+    return q.to(dtype), k.to(dtype), v.to(dtype)
 
 
 def make_head_qkv(

@@ -46,9 +46,17 @@ typedef struct CUstream_st* fa_stream_t;
 #define FA_VARIANT_OPT 1      /* lazy rescale (threshold 2^8), fp32 accumulation (default)  */
 #define FA_VARIANT_FP16ACC 2  /* P.V accumulated in fp16 per key tile, folded into fp32     */
 
+/* Element type of q, k, v and o (FaFwdParams.dtype). The reference takes float16 only
+ * (csrc/bindings.cpp:34); bfloat16 is an extension (its docs/fa3_fa4_techniques.md:22,90 list
+ * bf16 inputs as not done) that runs the baseline and opt variants, with P rounded to bfloat16
+ * for the P.V MMA and fp32 accumulation; FA_VARIANT_FP16ACC needs float16. */
+#define FA_DTYPE_FLOAT16 0
+#define FA_DTYPE_BFLOAT16 1
+
 /* Forward parameters (reference fa::FlashFwdParams, csrc/flash_fwd.h:18-30).
- * q, k, v, o: [batch, heads, seqlen, head_dim] fp16, contiguous, 16-byte aligned, on the
- * current CUDA device. o is written; the caller owns every buffer. */
+ * q, k, v, o: [batch, heads, seqlen, head_dim] of `dtype` (float16 unless set; all four the
+ * same type), contiguous, 16-byte aligned, on the current CUDA device. o is written; the
+ * caller owns every buffer. */
 typedef struct FaFwdParams {
     const void* q;
     const void* k;
@@ -61,13 +69,16 @@ typedef struct FaFwdParams {
     float softmax_scale;
     uint8_t causal;
     uint8_t variant; /* FA_VARIANT_* */
-    uint8_t reserved[2];
+    uint8_t dtype;   /* FA_DTYPE_* (0, float16, in a zero-initialised struct) */
+    uint8_t reserved;
 } FaFwdParams;
 
 /* Enqueues O = softmax(Q K^T * scale) V on `stream` (current device), one range of keys per
- * row block (fa_flash_fwd_auto may split key ranges). Asynchronous: no host synchronisation. Validates like the reference (batch, heads, seqlen > 0; head_dim 64/128;
- * batch*heads <= 65535; 16-byte aligned pointers; known variant) and returns
- * FA_ERR_INVALID_ARGUMENT with a message in fa_last_error() on failure.
+ * row block (fa_flash_fwd_auto may split key ranges). Asynchronous: no host synchronisation.
+ * Validates like the reference (batch, heads, seqlen > 0; head_dim 64/128; batch*heads <=
+ * 65535; 16-byte aligned pointers; known variant), plus a known dtype (float16 for
+ * FA_VARIANT_FP16ACC), and returns FA_ERR_INVALID_ARGUMENT with a message in fa_last_error()
+ * on failure.
  * Reference: fa::flash_fwd, csrc/kernels/flash_fwd.cu:625-652. */
 FA_API int fa_flash_fwd(const FaFwdParams* params, fa_stream_t stream);
 

@@ -25,6 +25,15 @@ REF_ATOL = 1e-2
 REF_RTOL = 1e-2
 
 
+# bfloat16 inputs (an extension of the reference): the same bounds scaled by the ratio of the
+# two formats' unit roundoffs, 2^-8 / 2^-11 = 8 (bf16 keeps 8 significant bits, fp16 11), since
+# every rounding on the path (inputs, P, O) is 8x coarser. With the bf16 floor (half an ulp of
+# |O| in [4, 8) is 1.56e-2) the max-abs bound is max(1.6e-2, bf16_floor + 8 * FP16_FLOOR_SLACK).
+BF16_FACTOR = 8.0
+MAX_ABS_BF16 = BF16_FACTOR * MAX_ABS_FP32
+MEAN_ABS_BF16 = BF16_FACTOR * MEAN_ABS_FP32
+
+
 class LiteralBoundMiss(UserWarning):
     """A fp32-variant case whose max-abs error exceeds the literal north_star bound (2e-3) but
     stays within fp16_floor + FP16_FLOOR_SLACK. pytest lists every one in its warnings summary,
@@ -43,6 +52,20 @@ def err_stats(out: torch.Tensor, ref: torch.Tensor) -> tuple[float, float]:
 def fp16_floor(ref: torch.Tensor) -> float:
     """Max error of the exact result merely rounded to fp16: no fp16 kernel can beat it."""
     return float((ref.half().float() - ref.float()).abs().max())
+
+
+def bf16_floor(ref: torch.Tensor) -> float:
+    """Max error of the exact result merely rounded to bfloat16."""
+    return float((ref.bfloat16().float() - ref.float()).abs().max())
+
+
+def check_tolerance_bf16(out, ref, label: str = "") -> tuple[float, float]:
+    mx, mean = err_stats(out, ref)
+    floor = bf16_floor(ref)
+    bound = max(MAX_ABS_BF16, floor + BF16_FACTOR * FP16_FLOOR_SLACK)
+    assert mx <= bound, f"{label} bf16 max-abs {mx:.3e} > {bound:.3e} (bf16 floor {floor:.3e})"
+    assert mean <= MEAN_ABS_BF16, f"{label} bf16 mean-abs {mean:.3e} > {MEAN_ABS_BF16}"
+    return mx, mean
 
 
 def check_tolerance(out, ref, variant: str, label: str = "") -> tuple[float, float]:

@@ -74,3 +74,24 @@ def test_forward_host_empty_sequence_needs_no_gpu():
     q = torch.zeros(2, 3, 0, 64, dtype=torch.float16)
     out = fa.forward_host(q, q, q)
     assert out.shape == q.shape
+
+
+def test_bf16_inputs_validate_before_touching_a_gpu():
+    import fa
+
+    q = torch.zeros(1, 1, 8, 64, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="same dtype"):
+        fa.forward_host(q, q.half(), q)
+    out = fa.forward_host(torch.zeros(2, 3, 0, 64, dtype=torch.bfloat16), torch.zeros(2, 3, 0, 64, dtype=torch.bfloat16),
+                          torch.zeros(2, 3, 0, 64, dtype=torch.bfloat16))
+    assert out.dtype == torch.bfloat16 and out.shape == (2, 3, 0, 64)
+
+
+def test_make_qkv_bf16_rounds_the_same_draws():
+    from fa.synthetic import make_qkv
+
+    qh, kh, vh = make_qkv(1, 2, 16, 64, seed=3)
+    qb, kb, vb = make_qkv(1, 2, 16, 64, seed=3, dtype=torch.bfloat16)
+    assert qb.dtype == torch.bfloat16
+    # both are roundings of the same fp32 values: within bf16's half ulp of the fp16 values
+    assert float((qb.float() - qh.float()).abs().max()) <= 2.0**-8 * float(qh.float().abs().max())

@@ -9,6 +9,7 @@ import subprocess
 from pathlib import Path
 
 import pytest
+import torch
 
 from fa import _C
 
@@ -40,17 +41,19 @@ def test_params_struct_layout_matches_c_header(tmp_path):
     src = tmp_path / "layout.c"
     src.write_text(
         '#include <stdio.h>\n#include <stddef.h>\n#include "fa_b200.h"\n'
-        "int main(void){printf(\"%zu %zu %zu %zu %zu %zu %zu %zu\\n\", sizeof(FaFwdParams),"
+        "int main(void){printf(\"%zu %zu %zu %zu %zu %zu %zu %zu %zu %d %d\\n\", sizeof(FaFwdParams),"
         " offsetof(FaFwdParams,o), offsetof(FaFwdParams,batch), offsetof(FaFwdParams,seqlen),"
         " offsetof(FaFwdParams,head_dim), offsetof(FaFwdParams,softmax_scale),"
-        " offsetof(FaFwdParams,causal), offsetof(FaFwdParams,variant)); return 0;}\n"
+        " offsetof(FaFwdParams,causal), offsetof(FaFwdParams,variant), offsetof(FaFwdParams,dtype),"
+        " FA_DTYPE_FLOAT16, FA_DTYPE_BFLOAT16); return 0;}\n"
     )
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-std=c99", "-I", str(REPO / "include"), "-o", str(exe), str(src)], check=True)
     got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
     P = _C.FaFwdParams
     want = [ctypes.sizeof(P), P.o.offset, P.batch.offset, P.seqlen.offset, P.head_dim.offset,
-            P.softmax_scale.offset, P.causal.offset, P.variant.offset]
+            P.softmax_scale.offset, P.causal.offset, P.variant.offset, P.dtype.offset,
+            _C.DTYPES[torch.float16], _C.DTYPES[torch.bfloat16]]
     assert got == want
 
 
@@ -73,6 +76,8 @@ def _params(**kw):
         (dict(batch=300, heads=300), "65535"),
         (dict(q=0x10002), "16-byte aligned"),
         (dict(variant=7), "unknown variant"),
+        (dict(dtype=2), "dtype must be FA_DTYPE_FLOAT16 or FA_DTYPE_BFLOAT16"),
+        (dict(dtype=1, variant=2), "fp16acc variant needs float16 inputs"),
     ],
 )
 def test_validation_rejects(kw, msg):
