@@ -8,13 +8,16 @@
  * program: no Python, no PyTorch, no C++ -- what a cgo / JNI / N-API binding would do.
  *
  *   capi_check                         the built-in case list (exit 0 when every case passes)
- *   capi_check B H N D CAUSAL VARIANT ITERS     one case, then ITERS timed launches
+ *   capi_check B H N D CAUSAL VARIANT ITERS [bf16]   one case, then ITERS timed launches
  *   capi_check --validate-only         argument validation only (needs no GPU)
  *
  * Per case: fp16 inputs from a seeded generator (xorshift64* + Box-Muller), device buffers from
  * cudaMalloc, fa_flash_fwd on a created stream, the watchdog word, the output against the
  * oracle (fp32 variants: max-abs <= max(2e-3, fp16 floor + 2.5e-4) and mean-abs <= 2e-4;
  * fp16acc: max-abs <= 1e-2), and a second launch that must reproduce the output bit for bit.
+ * bf16 cases (FaFwdParams.dtype = FA_DTYPE_BFLOAT16) draw bf16 values that fp16 also holds
+ * exactly (magnitudes below 2^-14 set to 0), so the same oracle checks them; their bounds are
+ * the fp16 ones times 8, the ratio of the two formats' unit roundoffs.
  */
 #include <cuda_runtime.h>
 #include <math.h>
@@ -93,6 +96,23 @@ static double half_bits_to_double(uint16_t h) {
 
 static double round_to_half(double x) { return half_bits_to_double(float_to_half_bits((float)x)); }
 
+/* binary32 -> bfloat16 bits (the high half), round to nearest even; finite inputs only. */
+static uint16_t float_to_bf16_bits(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    const uint32_t lsb = (x >> 16) & 1u;
+    return (uint16_t)((x + 0x7fffu + lsb) >> 16);
+}
+
+static double bf16_bits_to_double(uint16_t b) {
+    const uint32_t x = (uint32_t)b << 16;
+    float f;
+    memcpy(&f, &x, 4);
+    return (double)f;
+}
+
+static double round_to_bf16(double x) { return bf16_bits_to_double(float_to_bf16_bits((float)x)); }
+
 static const char* variant_name(int v) {
     return v == FA_VARIANT_BASELINE ? "baseline" : v == FA_VARIANT_OPT ? "opt" : "fp16acc";
 }
@@ -132,18 +152,41 @@ static int check_validation(void) {
         fprintf(stderr, "validation: variant 3 not rejected (%s)\n", fa_last_error());
         bad = 1;
     }
+    p.variant = FA_VARIANT_OPT;
+    p.dtype = 2;
+    if (fa_flash_fwd(&p, NULL) != FA_ERR_INVALID_ARGUMENT || strstr(fa_last_error(), "dtype") == NULL) {
+        fprintf(stderr, "validation: dtype 2 not rejected (%s)\n", fa_last_error());
+        bad = 1;
+    }
+    p.dtype = FA_DTYPE_BFLOAT16;
+    p.variant = FA_VARIANT_FP16ACC;
+    if (fa_flash_fwd(&p, NULL) != FA_ERR_INVALID_ARGUMENT || strstr(fa_last_error(), "fp16acc") == NULL) {
+        fprintf(stderr, "validation: bf16 fp16acc not rejected (%s)\n", fa_last_error());
+        bad = 1;
+    }
     printf("validation: %s\n", bad ? "FAILED" : "ok");
     return bad;
 }
 
-static int run_case(int b, int h, int n, int d, int causal, int variant, int iters, uint64_t seed) {
+static int run_case(int b, int h, int n, int d, int causal, int variant, int bf16, int iters, uint64_t seed) {
     const size_t elems = (size_t)b * h * n * d, bytes = elems * 2;
-    uint16_t* host[3];
+    uint16_t* host[3];  /* fp16 bits: the oracle's inputs */
+    uint16_t* dev_in[3];  /* the kernel's inputs: host[] itself, or the same values as bf16 bits */
     rng_state = seed * 0x9E3779B97F4A7C15ULL + 1;
     for (int t = 0; t < 3; ++t) {
         host[t] = (uint16_t*)malloc(bytes);
+        dev_in[t] = bf16 ? (uint16_t*)malloc(bytes) : host[t];
         for (size_t i = 0; i < elems; ++i) {
-            host[t][i] = float_to_half_bits((float)rng_normal());
+            if (bf16) {
+                uint16_t bb = float_to_bf16_bits((float)rng_normal());
+                if (fabs(bf16_bits_to_double(bb)) < ldexp(1.0, -14)) {
+                    bb = 0;
+                }
+                dev_in[t][i] = bb;
+                host[t][i] = float_to_half_bits((float)bf16_bits_to_double(bb));  /* exact */
+            } else {
+                host[t][i] = float_to_half_bits((float)rng_normal());
+            }
         }
     }
     void *dq, *dk, *dv, *dout;
@@ -151,9 +194,9 @@ static int run_case(int b, int h, int n, int d, int causal, int variant, int ite
     CHECK_CUDA(cudaMalloc(&dk, bytes));
     CHECK_CUDA(cudaMalloc(&dv, bytes));
     CHECK_CUDA(cudaMalloc(&dout, bytes));
-    CHECK_CUDA(cudaMemcpy(dq, host[0], bytes, cudaMemcpyHostToDevice));
-    CHECK_CUDA(cudaMemcpy(dk, host[1], bytes, cudaMemcpyHostToDevice));
-    CHECK_CUDA(cudaMemcpy(dv, host[2], bytes, cudaMemcpyHostToDevice));
+    CHECK_CUDA(cudaMemcpy(dq, dev_in[0], bytes, cudaMemcpyHostToDevice));
+    CHECK_CUDA(cudaMemcpy(dk, dev_in[1], bytes, cudaMemcpyHostToDevice));
+    CHECK_CUDA(cudaMemcpy(dv, dev_in[2], bytes, cudaMemcpyHostToDevice));
     cudaStream_t stream;
     CHECK_CUDA(cudaStreamCreate(&stream));
 
@@ -170,6 +213,7 @@ static int run_case(int b, int h, int n, int d, int causal, int variant, int ite
     p.softmax_scale = (float)(1.0 / sqrt((double)d));
     p.causal = (uint8_t)causal;
     p.variant = (uint8_t)variant;
+    p.dtype = (uint8_t)(bf16 ? FA_DTYPE_BFLOAT16 : FA_DTYPE_FLOAT16);
 
     int failed = 0;
     uint16_t* out = (uint16_t*)malloc(bytes);
@@ -204,21 +248,23 @@ static int run_case(int b, int h, int n, int d, int causal, int variant, int ite
     }
     double max_abs = 0.0, sum_abs = 0.0, floor_err = 0.0;
     for (size_t i = 0; i < elems; ++i) {
-        const double e = fabs(half_bits_to_double(out[i]) - ref[i]);
-        const double f = fabs(round_to_half(ref[i]) - ref[i]);
+        const double got = bf16 ? bf16_bits_to_double(out[i]) : half_bits_to_double(out[i]);
+        const double e = fabs(got - ref[i]);
+        const double f = fabs((bf16 ? round_to_bf16(ref[i]) : round_to_half(ref[i])) - ref[i]);
         max_abs = e > max_abs ? e : max_abs;
         floor_err = f > floor_err ? f : floor_err;
         sum_abs += e;
     }
     const double mean_abs = sum_abs / (double)elems;
     const int acc16 = variant == FA_VARIANT_FP16ACC;
-    const double bound = acc16 ? 1e-2 : fmax(2e-3, floor_err + 2.5e-4);
-    if (!(max_abs <= bound) || (!acc16 && !(mean_abs <= 2e-4))) {
+    const double k = bf16 ? 8.0 : 1.0;  /* bf16: the fp16 bounds times 2^-8 / 2^-11 */
+    const double bound = acc16 ? 1e-2 : fmax(k * 2e-3, floor_err + k * 2.5e-4);
+    if (!(max_abs <= bound) || (!acc16 && !(mean_abs <= k * 2e-4))) {
         failed = 1;
     }
-    printf("B%d H%d N%d D%d %s %-8s max-abs %.3e (bound %.3e, fp16 floor %.3e) mean-abs %.3e %s\n", b, h, n,
-           d, causal ? "causal" : "full  ", variant_name(variant), max_abs, bound, floor_err, mean_abs,
-           failed ? "FAILED" : "ok");
+    printf("B%d H%d N%d D%d %s %-8s %s max-abs %.3e (bound %.3e, %s floor %.3e) mean-abs %.3e %s\n", b, h,
+           n, d, causal ? "causal" : "full  ", variant_name(variant), bf16 ? "bf16" : "fp16", max_abs, bound,
+           bf16 ? "bf16" : "fp16", floor_err, mean_abs, failed ? "FAILED" : "ok");
 
     if (iters > 0 && !failed) {
         cudaEvent_t e0, e1;
@@ -245,6 +291,9 @@ static int run_case(int b, int h, int n, int d, int causal, int variant, int ite
     free(out);
     free(out2);
     for (int t = 0; t < 3; ++t) {
+        if (dev_in[t] != host[t]) {
+            free(dev_in[t]);
+        }
         free(host[t]);
     }
     cudaFree(dq);
@@ -260,23 +309,24 @@ int main(int argc, char** argv) {
     if (argc == 2 && strcmp(argv[1], "--validate-only") == 0) {
         return failed ? 1 : 0;
     }
-    if (argc == 8) {
+    if (argc == 8 || argc == 9) {
         failed |= run_case(atoi(argv[1]), atoi(argv[2]), atoi(argv[3]), atoi(argv[4]), atoi(argv[5]),
-                           atoi(argv[6]), atoi(argv[7]), 42);
+                           atoi(argv[6]), argc == 9 && strcmp(argv[8], "bf16") == 0, atoi(argv[7]), 42);
     } else if (argc == 1) {
-        static const int cases[][6] = {
-            /* B, H, N, D, causal, variant */
-            {1, 2, 300, 128, 1, FA_VARIANT_OPT},     {2, 3, 257, 64, 0, FA_VARIANT_BASELINE},
-            {1, 2, 1000, 128, 1, FA_VARIANT_FP16ACC}, {1, 1, 1, 64, 0, FA_VARIANT_OPT},
-            {2, 2, 513, 128, 0, FA_VARIANT_OPT},     {1, 3, 640, 64, 1, FA_VARIANT_FP16ACC},
-            {1, 1, 2500, 128, 0, FA_VARIANT_BASELINE},
+        static const int cases[][7] = {
+            /* B, H, N, D, causal, variant, bf16 */
+            {1, 2, 300, 128, 1, FA_VARIANT_OPT, 0},     {2, 3, 257, 64, 0, FA_VARIANT_BASELINE, 0},
+            {1, 2, 1000, 128, 1, FA_VARIANT_FP16ACC, 0}, {1, 1, 1, 64, 0, FA_VARIANT_OPT, 0},
+            {2, 2, 513, 128, 0, FA_VARIANT_OPT, 0},     {1, 3, 640, 64, 1, FA_VARIANT_FP16ACC, 0},
+            {1, 1, 2500, 128, 0, FA_VARIANT_BASELINE, 0}, {1, 2, 700, 128, 1, FA_VARIANT_OPT, 1},
+            {2, 2, 385, 64, 0, FA_VARIANT_BASELINE, 1},
         };
         for (size_t i = 0; i < sizeof(cases) / sizeof(cases[0]); ++i) {
             const int* c = cases[i];
-            failed |= run_case(c[0], c[1], c[2], c[3], c[4], c[5], 0, 1234 + i);
+            failed |= run_case(c[0], c[1], c[2], c[3], c[4], c[5], c[6], 0, 1234 + i);
         }
     } else {
-        fprintf(stderr, "usage: %s [B H N D CAUSAL VARIANT ITERS]\n", argv[0]);
+        fprintf(stderr, "usage: %s [B H N D CAUSAL VARIANT ITERS [bf16]]\n", argv[0]);
         return 2;
     }
     printf("capi_check: %s\n", failed ? "FAILED" : "all cases passed");
