@@ -16,8 +16,9 @@ over the whole problem (every rank's shard); value = the problem's FLOPs / the m
 of the event-timed duration. The same line carries the non-causal twin (cfg3nc) on the same
 shards, at N > 1 the weak-scaling figure (every rank a private copy of config 1), and at N = 1
 `per_config`: configs 1 and 2 (fp32 and fp16 accumulation), configs 3 (causal) and 2 with
-bfloat16 inputs, and rows of the ragged sweep (config 4), each event-timed for K steps with its
-clocks.
+bfloat16 inputs, config 3 (causal and non-causal) with e4m3 inputs (fa.forward_fp8; its
+fraction is of the fp16 peak like every other row, e4m3's tensor peak being twice that), and
+rows of the ragged sweep (config 4), each event-timed for K steps with its clocks.
 
 `value` is timed on the device with CUDA events around exactly K steps with inputs resident in
 HBM (inputs larger than L2); `e2e` is the same metric through the public API with host
@@ -59,7 +60,7 @@ PKG = REPO / "flash-attention-from-scratch_b200"
 
 METRIC = "attn fwd TFLOPS (fp16, d=64/128, causal+non) at 1/2/4/8 B200; % of TC peak"
 HEADLINE = "cfg3"
-PER_CONFIG = ["cfg1", "cfg2", "cfg2acc", "cfg3bf16", "cfg2bf16", "cfg4:8191:128:1", "cfg4:12345:128:0", "cfg4:12345:64:1",
+PER_CONFIG = ["cfg1", "cfg2", "cfg2acc", "cfg3bf16", "cfg2bf16", "cfg3fp8", "cfg3ncfp8", "cfg4:8191:128:1", "cfg4:12345:128:0", "cfg4:12345:64:1",
               "cfg4:3000:128:0", "cfg4:1000:128:1", "cfg4:1000:64:0"]
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
@@ -99,6 +100,10 @@ def workload(name: str) -> dict:
     if name.endswith("bf16") and name[: -len("bf16")] in syn.CONFIGS:
         # a configuration's shape and values with bfloat16 inputs (an extension of the reference)
         return dict(syn.CONFIGS[name[: -len("bf16")]], outliers=False, variant="opt", dtype="bf16", name=name)
+    if name in ("cfg3fp8", "cfg3ncfp8"):
+        # config 3 with e4m3 inputs (per-tensor descales; fp16 O), causal / non-causal
+        return dict(syn.CONFIGS["cfg3"], causal=(name == "cfg3fp8"), outliers=False, variant="opt", dtype="fp8",
+                    name=name)
     if name.startswith("cfg4:"):
         # cfg4:N:d:causal, e.g. cfg4:12345:128:1 (B16 H16, seed 4, outlier channel)
         _, n, d, causal = name.split(":")
@@ -670,23 +675,30 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                 oc = syn.outlier_channels(pc["d"])
                 pq[..., :oc] *= 8.0
                 pk[..., :oc] *= 8.0
-            pdt = torch.bfloat16 if pc.get("dtype") == "bf16" else torch.float16
-            pq, pk, pv = pq.to(pdt), pk.to(pdt), pv.to(pdt)
+            if pc.get("dtype") == "fp8":
+                (pq, qs), (pk, ks), (pv, vs) = (fa.quantize_fp8(t) for t in (pq, pk, pv))
 
-            def pc_step():
-                return _C.forward(pq, pk, pv, pc["causal"], None, pc["variant"])
+                def pc_step():
+                    return _C.forward_fp8(pq, pk, pv, qs, ks, vs, pc["causal"], None, pc["variant"])
+            else:
+                pdt = torch.bfloat16 if pc.get("dtype") == "bf16" else torch.float16
+                pq, pk, pv = pq.to(pdt), pk.to(pdt), pv.to(pdt)
+
+                def pc_step():
+                    return _C.forward(pq, pk, pv, pc["causal"], None, pc["variant"])
 
             p_ms, p_clocks = timed(pc_step, args.steps, args.warmup, True)
             check_status()
             p_val = flops_of(pc) / (p_ms * 1e-3) / 1e12
-            io = 4 * pq.numel() * 2
+            io = 4 * pq.numel() * 2 if pc.get("dtype") != "fp8" else pq.numel() * (3 + 2 + 2)  # fp8: q, k, v, V^T out/in, O
             per_config[name] = {
                 "B": pc["b"], "H": pc["h"], "N": pc["n"], "d": pc["d"], "causal": pc["causal"],
                 "variant": pc["variant"], "dtype": pc.get("dtype", "f16"), "outliers": bool(pc.get("outliers")),
                 "value": p_val, "unit": "TFLOPS",
                 "ms_per_step": p_ms, "frac": p_val / peak, "hbm_gbs_algorithmic": io / (p_ms * 1e-3) / 1e9,
-                "kernels_per_launch": kernels_per_launch(pq, pk, pv, pc["causal"], pc["variant"]),
-                "plan": plan_of(pq, pc["causal"], pc["variant"]),
+                "kernels_per_launch": (2 if pc.get("dtype") == "fp8"  # V transpose + attention
+                                       else kernels_per_launch(pq, pk, pv, pc["causal"], pc["variant"])),
+                "plan": None if pc.get("dtype") == "fp8" else plan_of(pq, pc["causal"], pc["variant"]),
                 "traffic": traffic_per_launch(name), "clocks": p_clocks, "steps": args.steps,
             }
             del pq, pk, pv

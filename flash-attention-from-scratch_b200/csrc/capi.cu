@@ -93,8 +93,13 @@ int validate(const FaFwdParams* p) {
     if (p->variant > FA_VARIANT_FP16ACC) {
         return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd: unknown variant");
     }
-    if (p->dtype > FA_DTYPE_BFLOAT16) {
-        return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd: dtype must be FA_DTYPE_FLOAT16 or FA_DTYPE_BFLOAT16");
+    if (p->dtype > FA_DTYPE_FLOAT8_E4M3) {
+        return fail(FA_ERR_INVALID_ARGUMENT,
+                    "flash_fwd: dtype must be FA_DTYPE_FLOAT16, FA_DTYPE_BFLOAT16 or FA_DTYPE_FLOAT8_E4M3");
+    }
+    if (p->dtype == FA_DTYPE_FLOAT8_E4M3 && (p->head_dim != 128 || p->variant == FA_VARIANT_FP16ACC)) {
+        return fail(FA_ERR_INVALID_ARGUMENT,
+                    "flash_fwd: float8 inputs need head_dim 128 and the baseline or opt variant");
     }
     if (p->dtype == FA_DTYPE_BFLOAT16 && p->variant == FA_VARIANT_FP16ACC) {
         // kind::f16 MMAs accumulate bfloat16 products in fp32 only; the fp16 partials of
@@ -113,10 +118,13 @@ fa_sm100::Plan plan_for(const FaFwdParams* p, int num_splits, int sm_count) {
 }
 
 int launch_one(const FaFwdParams* p, cudaStream_t stream, int num_splits, void* workspace,
-               uint64_t workspace_bytes) {
+               uint64_t workspace_bytes, const Fp8Extra* fp8) {
     const int rc = validate(p);
     if (rc != FA_OK) {
         return rc;
+    }
+    if ((p->dtype == FA_DTYPE_FLOAT8_E4M3) != (fp8 != nullptr) || (fp8 != nullptr && num_splits != 1)) {
+        return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd: float8 inputs go through fa_flash_fwd_fp8");
     }
     if (num_splits < 0 || num_splits > kMaxSplits) {
         return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd_splitkv: num_splits must be in 1 .. 64, got " +
@@ -154,10 +162,16 @@ int launch_one(const FaFwdParams* p, cudaStream_t stream, int num_splits, void* 
     prob.causal = p->causal != 0;
     prob.variant = p->variant;
     prob.bf16 = p->dtype == FA_DTYPE_BFLOAT16;
+    prob.fp8 = fp8 != nullptr;
+    prob.vt = prob.fp8 ? fp8->vt : nullptr;
+    prob.vt_cols = (p->seqlen + 15) / 16 * 16;
     fa_sm100::FwdArgs args{};
     args.seqlen = p->seqlen;
     args.num_bh = bh;
-    args.scale_log2 = static_cast<float>(static_cast<double>(p->softmax_scale) * M_LOG2E);
+    // fp8: the scores of the e4m3 values carry q_descale * k_descale.
+    const double qk_descale = prob.fp8 ? static_cast<double>(fp8->q_descale) * fp8->k_descale : 1.0;
+    args.scale_log2 = static_cast<float>(static_cast<double>(p->softmax_scale) * qk_descale * M_LOG2E);
+    args.out_scale = prob.fp8 ? fp8->v_descale : 1.0f;
     args.epoch = next_epoch();
     args.status = status;
     args.rows_pad = (p->seqlen + 255) / 256 * 256;
@@ -165,6 +179,12 @@ int launch_one(const FaFwdParams* p, cudaStream_t stream, int num_splits, void* 
         const uint64_t records = plan.workspace_bytes / (static_cast<uint64_t>(p->head_dim + 2) * 4u);
         args.ws_o = static_cast<float*>(workspace);
         args.ws_ml = args.ws_o + records * p->head_dim;
+    }
+    if (prob.fp8) {
+        err = fa_sm100::launch_fp8_transpose_v(p->v, fp8->vt, bh, p->seqlen, stream);
+        if (err != cudaSuccess) {
+            return cuda_fail(err, "fp8 V transpose launch");
+        }
     }
     err = fa_sm100::launch_forward(prob, args, plan, stream);
     if (err == cudaErrorInvalidValue) {
@@ -324,6 +344,40 @@ int fa_flash_fwd_splitkv(const FaFwdParams* params, int32_t num_splits, void* wo
     }
     return launch_one(params, reinterpret_cast<cudaStream_t>(stream), num_splits, workspace,
                       workspace_bytes);
+}
+
+int fa_fp8_workspace_size(const FaFwdParams* params, uint64_t* bytes_out) {
+    const int rc = validate(params);
+    if (rc != FA_OK) {
+        return rc;
+    }
+    if (params->dtype != FA_DTYPE_FLOAT8_E4M3) {
+        return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd_fp8: params->dtype must be FA_DTYPE_FLOAT8_E4M3");
+    }
+    if (bytes_out != nullptr) {
+        *bytes_out = fa_sm100::fp8_vt_bytes(params->batch * params->heads, params->seqlen, params->head_dim);
+    }
+    fa_capi::clear_error();
+    return FA_OK;
+}
+
+int fa_flash_fwd_fp8(const FaFwdParams* params, float q_descale, float k_descale, float v_descale,
+                     void* workspace, uint64_t workspace_bytes, fa_stream_t stream) {
+    uint64_t need = 0;
+    const int rc = fa_fp8_workspace_size(params, &need);
+    if (rc != FA_OK) {
+        return rc;
+    }
+    if (!(q_descale > 0.0f) || !(k_descale > 0.0f) || !(v_descale > 0.0f) || !std::isfinite(q_descale) ||
+        !std::isfinite(k_descale) || !std::isfinite(v_descale)) {
+        return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd_fp8: descales must be positive and finite");
+    }
+    if (workspace == nullptr || workspace_bytes < need || !fa_capi::aligned16(workspace)) {
+        return fail(FA_ERR_INVALID_ARGUMENT, "flash_fwd_fp8: workspace must be 16-byte aligned and hold at least " +
+                                                 std::to_string(need) + " bytes");
+    }
+    const fa_capi::Fp8Extra extra{q_descale, k_descale, v_descale, workspace};
+    return launch_one(params, reinterpret_cast<cudaStream_t>(stream), 1, nullptr, 0, &extra);
 }
 
 int fa_kernel_info(int32_t head_dim, int32_t variant, int32_t* smem_bytes, int32_t* threads) {

@@ -32,10 +32,20 @@ int validate(const FaFwdParams* p);
 // last partial wave).
 fa_sm100::Plan plan_for(const FaFwdParams* p, int num_splits, int sm_count);
 
+// fp8 launch extras: per-tensor descales and the transposed-V workspace.
+struct Fp8Extra {
+    float q_descale;
+    float k_descale;
+    float v_descale;
+    void* vt;
+};
+
 // Validates, plans (num_splits as in plan_for), encodes the tensor maps and enqueues the forward
 // plus, when the plan splits key ranges, the combine, with `workspace` holding the partials.
+// e4m3 inputs (p->dtype == FA_DTYPE_FLOAT8_E4M3) need `fp8` (and num_splits == 1); the
+// transpose of V into fp8->vt is enqueued first.
 int launch_one(const FaFwdParams* p, cudaStream_t stream, int num_splits, void* workspace,
-               uint64_t workspace_bytes);
+               uint64_t workspace_bytes, const Fp8Extra* fp8 = nullptr);
 
 // Device address of a module variable, looked up per device with that device current and
 // cached for the device's current context (a device reset replaces the context, which voids

@@ -73,6 +73,7 @@ struct FwdArgs {
     float* ws_ml;         // split records x 2 fp32: m (log2 units), l
     int num_items;        // work items, set by the launcher
     void* o;              // output [num_bh][seqlen][D] fp16 / bf16, set by the launcher
+    float out_scale;      // fp8: O is multiplied by V's descale in the epilogue (else unused)
 };
 
 // Split-KV workspace bytes for a problem (16-byte aligned sections).
@@ -125,7 +126,19 @@ struct FwdProblem {
     bool causal;
     int variant;
     bool bf16;
+    // fp8 (e4m3 q, k, v; fp16 o): vt is V transposed, [num_bh][D][vt_cols] e4m3 with keys
+    // contiguous and vt_cols = seqlen rounded up to 16 (zeros beyond seqlen).
+    bool fp8;
+    const void* vt;
+    int vt_cols;
 };
+
+// fp8: bytes of the transposed-V workspace for a problem, and the launch that fills it from V
+// ([num_bh][seqlen][128] e4m3) on `stream`.
+inline unsigned long long fp8_vt_bytes(int num_bh, int seqlen, int head_dim) {
+    return static_cast<unsigned long long>(num_bh) * head_dim * ((seqlen + 15) / 16 * 16);
+}
+cudaError_t launch_fp8_transpose_v(const void* v, void* vt, int num_bh, int seqlen, cudaStream_t stream);
 
 // Unique id (cuCtxGetId, plus one) of the calling thread's current CUDA context, or 0 when
 // no context is current or the driver lacks the call. Values the library caches per device

@@ -102,11 +102,11 @@ namespace fa_sm100 {
 
 constexpr int kBM = 128;             // query rows per tile (= TMEM lanes = MMA M)
 constexpr int kBN = 128;             // keys per K/V tile (= MMA N of Q K^T)
-constexpr int kBoxBytes = 128 * 128; // one TMA box: 128 rows x 64 fp16 (128 B, one swizzle span)
+constexpr int kBoxBytes = 128 * 128; // one TMA box: 128 rows x 128 B (64 fp16 or 128 e4m3; one swizzle span)
 constexpr int kPersistentMaxN = 2048; // persistent grid (one CTA per SM walks the items) up to this N
 constexpr int kPersistentMaxNFull = 8192;  // ... and up to this N without the causal mask
 
-template <int D_, bool CAUSAL_, int VARIANT_, bool BF16_ = false>
+template <int D_, bool CAUSAL_, int VARIANT_, bool BF16_ = false, bool FP8_ = false>
 struct FwdCfg {
     static constexpr int D = D_;
     static constexpr bool CAUSAL = CAUSAL_;
@@ -116,6 +116,12 @@ struct FwdCfg {
     // fp16acc variant is float16 only.
     static constexpr bool BF16 = BF16_;
     static_assert(!(BF16_ && VARIANT_ == kVariantFp16Acc), "fp16acc needs float16 operands");
+    // e4m3 Q, K, V (per-tensor descales applied on the host side of the scores and in the
+    // epilogue), P rounded to e4m3 in TMEM, kind::f8f6f4 MMAs with fp32 accumulation, fp16 O.
+    // V arrives transposed ([B*H][D][N], keys contiguous), so that both MMAs read K-major
+    // operands. d = 128 and the fp32-accumulating variants only.
+    static constexpr bool FP8 = FP8_;
+    static_assert(!FP8_ || (D_ == 128 && VARIANT_ != kVariantFp16Acc && !BF16_), "fp8: d = 128, fp32 accumulation");
     // fp16acc (reference ACC16, flash_fwd.cu:439-470): P.V of each 128-key tile accumulated in
     // fp16 into a fresh partial T_t, which the softmax folds into the fp32 O_t. Exact max (no
     // lazy rescale), so p <= 1. P is stored as p * 2^-kAccShift, which bounds |T_t| by
@@ -126,7 +132,12 @@ struct FwdCfg {
     static constexpr int kAccShift = ACC16 ? (D == 64 ? 2 : 1) : 0;
     // Lazy rescale (reference LAZY, flash_fwd.cu:365-376): keep a stale row max until the
     // tile max exceeds it by more than 2^8. Threshold 0 = exact running max.
-    static constexpr float kRescaleThreshold = (VARIANT_ == kVariantOpt) ? 8.0f : 0.0f;
+    // fp8: P is stored as p * 2^(8 - threshold) so that, with p <= 2^threshold under the lazy
+    // rule, the stored value stays within e4m3's range (448) and small p keep more bits; the
+    // lazy threshold is 4 there (p * 2^4 <= 256).
+    static constexpr float kRescaleThreshold =
+        (VARIANT_ == kVariantOpt) ? (FP8_ ? 4.0f : 8.0f) : 0.0f;
+    static constexpr float kPLog2Scale = FP8_ ? 8.0f - kRescaleThreshold : 0.0f;
     // Query tiles per CTA. fp16acc at d = 128 needs S + O + T = 384 columns for one tile; it
     // spends the remaining 128 on a second S buffer (kSBufs): S(j+1) is computed while the
     // softmax works on tile j, and the fold of T(j) waits until the end of tile j+1, so no
@@ -136,16 +147,24 @@ struct FwdCfg {
     static constexpr bool SEP_P = !ACC16 && D == 64;
     static constexpr int kEmuPer8 = (D == 128) ? FA_EMU_PER8_D128 : FA_EMU_PER8_D64;
     static constexpr int kPolyDeg = (D == 128) ? FA_EXP_POLY_DEG_D128 : FA_EXP_POLY_DEG_D64;
-    static constexpr int kTileBytes = kBM * D * 2;  // one Q, K, V or O tile (BM == BN)
-    static constexpr int kBoxes = D / 64;           // TMA boxes per tile
-    static constexpr int STAGES = (D == 128) ? 4 : FA_STAGES_D64;
+    static constexpr int kElemBytes = FP8 ? 1 : 2;
+    static constexpr int kTileBytes = kBM * D * kElemBytes;  // one Q, K or V tile (BM == BN)
+    static constexpr int kOutTileBytes = kBM * D * 2;        // one O tile (fp16 / bf16)
+    // A Q buffer also stages its tile's O for the TMA store.
+    static constexpr int kQTileBytes = kTileBytes > kOutTileBytes ? kTileBytes : kOutTileBytes;
+    static constexpr int kBoxes = D * kElemBytes / 128;       // TMA boxes per Q, K or V tile
+    static constexpr int kBoxElems = 128 / kElemBytes;        // elements per box row
+    static constexpr int kOutBoxes = D / 64;                  // TMA boxes per O tile
+    static constexpr int kKSteps = D * kElemBytes / 32;       // MMA K steps of Q K^T (32 B each)
+    static constexpr int kPvSteps = kBN * kElemBytes / 32;    // MMA K steps of P V
+    static constexpr int STAGES = FP8 ? 8 : ((D == 128) ? 4 : FA_STAGES_D64);
     static_assert(STAGES <= 16, "K/V ring barriers");
     // Shared memory (offsets from a 1024-byte aligned base).
     static constexpr int kSmemQ = 0;
-    static constexpr int kSmemKV = NQ * kTileBytes;
+    static constexpr int kSmemKV = NQ * kQTileBytes;
     // O staging tile of the persistent grid's epilogue (the Q buffers hold the next item's Q).
     static constexpr int kSmemStage = kSmemKV + STAGES * kTileBytes;
-    static constexpr int kSmemBytes = kSmemStage + kTileBytes;
+    static constexpr int kSmemBytes = kSmemStage + kOutTileBytes;
     static constexpr int kSmemAlloc = kSmemBytes + 1024;
     // Tensor memory columns.
     static constexpr int kTmemS = 0;
@@ -214,11 +233,16 @@ __device__ __forceinline__ float f16cell_to_float(uint32_t cell) {
 // tile's first byte.
 template <class Cfg>
 __device__ __forceinline__ void issue_s_mma(uint32_t tmem_s, uint64_t qd, uint64_t kd) {
+    // kind::f8f6f4 with e4m3 A and B (format code 0) has the bit layout of kind::f16 with f16.
     constexpr uint32_t idesc = make_idesc_f16(kBM, kBN, /*d_f32=*/true, /*b_mn_major=*/false, Cfg::BF16);
 #pragma unroll
-    for (int kk = 0; kk < Cfg::D / 16; ++kk) {
+    for (int kk = 0; kk < Cfg::kKSteps; ++kk) {
         const uint64_t off = static_cast<uint64_t>(((kk / 4) * kBoxBytes + (kk % 4) * 32) >> 4);
-        umma_ss(tmem_s, qd + off, kd + off, idesc, kk > 0 ? 1u : 0u);
+        if constexpr (Cfg::FP8) {
+            umma_ss_f8(tmem_s, qd + off, kd + off, idesc, kk > 0 ? 1u : 0u);
+        } else {
+            umma_ss(tmem_s, qd + off, kd + off, idesc, kk > 0 ? 1u : 0u);
+        }
     }
 }
 
@@ -226,6 +250,16 @@ __device__ __forceinline__ void issue_s_mma(uint32_t tmem_s, uint64_t qd, uint64
 template <class Cfg>
 __device__ __forceinline__ void issue_pv_mma_f32(uint32_t tmem_o, uint32_t tmem_p, uint64_t vd,
                                                  bool first) {
+    if constexpr (Cfg::FP8) {
+        // fp8: V^T tile K-major (keys contiguous, like a K tile), P four e4m3 per column.
+        constexpr uint32_t idesc8 = make_idesc_f16(kBM, Cfg::D, /*d_f32=*/true, /*b_mn_major=*/false);
+#pragma unroll
+        for (int kk = 0; kk < Cfg::kPvSteps; ++kk) {
+            umma_ts_f8(tmem_o, tmem_p + kk * 8, vd + static_cast<uint64_t>((kk * 32) >> 4), idesc8,
+                       (first && kk == 0) ? 0u : 1u);
+        }
+        return;
+    }
     constexpr uint32_t idesc = make_idesc_f16(kBM, Cfg::D, /*d_f32=*/true, /*b_mn_major=*/true, Cfg::BF16);
 #pragma unroll
     for (int kk = 0; kk < kBN / 16; ++kk) {
@@ -549,8 +583,11 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 
                 // Probabilities, packed fp16 pairs, into P_t.
                 const float2 mul2 = make_float2(mul, mul);
-                // fp16acc stores p * 2^-kAccShift: the shift joins the max in the exponent.
-                const float neg = (Cfg::kAccShift != 0) ? -max_used - static_cast<float>(Cfg::kAccShift) : -max_used;
+                // fp16acc stores p * 2^-kAccShift, fp8 p * 2^kPLog2Scale: the shift joins the max
+                // in the exponent.
+                const float neg = Cfg::FP8 ? Cfg::kPLog2Scale - max_used
+                                           : ((Cfg::kAccShift != 0) ? -max_used - static_cast<float>(Cfg::kAccShift)
+                                                                    : -max_used);
                 const float2 neg2 = make_float2(neg, neg);
                 float2 sum2[4];
 #pragma unroll
@@ -558,7 +595,25 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     sum2[i] = make_float2(0.0f, 0.0f);
                 }
 #pragma unroll
-                for (int chunk = 0; chunk < NC / 64; ++chunk) {
+                for (int chunk = 0; chunk < NC / 64 && Cfg::FP8; ++chunk) {
+                    // fp8: the 64 keys of the chunk become 16 columns of four e4m3 each (key
+                    // 4w + b in byte b of column w); the row sum adds the rounded values.
+                    uint32_t pk8[16];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const int c = chunk * 64 + 2 * i;
+                        const float2 x2 = __ffma2_rn(make_float2(u2f(sr[c]), u2f(sr[c + 1])), mul2, neg2);
+                        const float2 e = ((i % 8) < Cfg::kEmuPer8)
+                                             ? (Cfg::kPolyDeg == 3 ? exp2_poly2_deg3(x2) : exp2_poly2(x2))
+                                             : make_float2(ex2_approx(x2.x), ex2_approx(x2.y));
+                        const uint32_t b = pack_e4m3x2(e.x, e.y);
+                        pk8[i / 2] = (i & 1) ? (pk8[i / 2] | (b << 16)) : b;
+                        add_x2_to_f32<false>(sum2[i % 4].x, sum2[i % 4].y, e4m3x2_to_half2(b));
+                    }
+                    tmem_st16(t_p + s_off + chunk * 16, pk8);
+                }
+#pragma unroll
+                for (int chunk = 0; chunk < NC / 64 && !Cfg::FP8; ++chunk) {
                     uint32_t pk[32];
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
@@ -711,10 +766,13 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                         make_float2(nt > 0 ? row_max : -INFINITY, nt > 0 ? row_sum : 0.0f);
                 }
             } else if (tma_store_o && ok && nt > 0) {
-                const float inv_sum = (row_sum > 0.0f) ? (1.0f / row_sum) : 0.0f;
+                float inv_sum = (row_sum > 0.0f) ? (1.0f / row_sum) : 0.0f;
+                if constexpr (Cfg::FP8) {
+                    inv_sum *= args.out_scale;  // V's descale
+                }
                 // Stage O (fp16) in this tile's Q buffer, in the swizzled layout of the TMA box.
                 // Every MMA that read Q_t has completed (its S was consumed above).
-                uint8_t* out = smem + Cfg::kSmemQ + t * Cfg::kTileBytes;
+                uint8_t* out = smem + Cfg::kSmemQ + t * Cfg::kQTileBytes;
 #pragma unroll
                 for (int c = 0; c < D / 32; ++c) {
                     uint32_t o[32];
@@ -744,7 +802,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 if (row == 0) {
                     if (mbar_wait(smem_u32(&sb.epi[t]), 0, wctx, kStatusTimeoutEpilogue)) {
 #pragma unroll
-                        for (int b = 0; b < Cfg::kBoxes; ++b) {
+                        for (int b = 0; b < Cfg::kOutBoxes; ++b) {
                             tma_store_3d(&tm_o, smem_u32(out) + b * kBoxBytes, b * 64, q0, it.bh);
                         }
                         tma_store_commit();
@@ -765,7 +823,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 }
                 uint8_t* out = smem + Cfg::kSmemStage;
                 if (turn && nt > 0) {
-                    const float inv_sum = (row_sum > 0.0f) ? (1.0f / row_sum) : 0.0f;
+                    float inv_sum = (row_sum > 0.0f) ? (1.0f / row_sum) : 0.0f;
+                    if constexpr (Cfg::FP8) {
+                        inv_sum *= args.out_scale;
+                    }
 #pragma unroll
                     for (int c = 0; c < D / 32; ++c) {
                         uint32_t o[32];
@@ -798,7 +859,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                     if (mbar_wait(smem_u32(&sb.epi[t]), stg_items & 1, wctx, kStatusTimeoutEpilogue) && turn &&
                         nt > 0) {
 #pragma unroll
-                        for (int b = 0; b < Cfg::kBoxes; ++b) {
+                        for (int b = 0; b < Cfg::kOutBoxes; ++b) {
                             tma_store_3d(&tm_o, smem_u32(out) + b * kBoxBytes, b * 64, q0, it.bh);
                         }
                         tma_store_commit();
@@ -848,8 +909,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                             mbar_arrive_expect_tx(bar, Cfg::kTileBytes);
 #pragma unroll
                             for (int b = 0; b < Cfg::kBoxes; ++b) {
-                                tma_load_3d(smem_base + Cfg::kSmemQ + t * Cfg::kTileBytes + b * kBoxBytes,
-                                            &tm_q, bar, b * 64, it.q_row0 + t * kBM, it.bh);
+                                tma_load_3d(smem_base + Cfg::kSmemQ + t * Cfg::kQTileBytes + b * kBoxBytes,
+                                            &tm_q, bar, b * Cfg::kBoxElems, it.q_row0 + t * kBM, it.bh);
                             }
                             ++q_loads[t];
                         }
@@ -868,10 +929,16 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                         const uint32_t bar = smem_u32(&sb.kv_full[stage]);
                         mbar_arrive_expect_tx(bar, Cfg::kTileBytes);
                         const CUtensorMap* map = (kind == 0) ? &tm_k : &tm_v;
+                        if (Cfg::FP8 && kind == 1) {
+                            // V^T: [B*H][D][keys], one box of 128 keys x D rows.
+                            tma_load_3d(smem_base + Cfg::kSmemKV + stage * Cfg::kTileBytes, map, bar,
+                                        (it.kv0 + j) * kBN, 0, it.bh);
+                        } else {
 #pragma unroll
-                        for (int b = 0; b < Cfg::kBoxes; ++b) {
-                            tma_load_3d(smem_base + Cfg::kSmemKV + stage * Cfg::kTileBytes + b * kBoxBytes,
-                                        map, bar, b * 64, (it.kv0 + j) * kBN, it.bh);
+                            for (int b = 0; b < Cfg::kBoxes; ++b) {
+                                tma_load_3d(smem_base + Cfg::kSmemKV + stage * Cfg::kTileBytes + b * kBoxBytes,
+                                            map, bar, b * Cfg::kBoxElems, (it.kv0 + j) * kBN, it.bh);
+                            }
                         }
                         loaded[stage] = true;
                         last_parity[stage] = phase;
@@ -906,7 +973,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             const int t = (warp == Cfg::kMmaWarp) ? 0 : 1;
             bool ok = true;
             const uint32_t kv_addr0 = smem_base + Cfg::kSmemKV;
-            const uint64_t qd = make_desc_kmajor_sw128(smem_base + Cfg::kSmemQ + t * Cfg::kTileBytes);
+            const uint64_t qd = make_desc_kmajor_sw128(smem_base + Cfg::kSmemQ + t * Cfg::kQTileBytes);
             const uint64_t kd0 = make_desc_kmajor_sw128(kv_addr0);
             const uint64_t vd0 = make_desc_mnmajor_sw128(kv_addr0, kBoxBytes);
             auto stage_off = [](int stage) -> uint64_t {
@@ -1132,10 +1199,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             const uint32_t kv_addr0 = smem_base + Cfg::kSmemKV;
             const uint64_t qd0 = make_desc_kmajor_sw128(q_addr0);
             auto q_desc = [qd0](int t) -> uint64_t {
-                return qd0 + static_cast<uint64_t>(t * (Cfg::kTileBytes >> 4));
+                return qd0 + static_cast<uint64_t>(t * (Cfg::kQTileBytes >> 4));
             };
             const uint64_t kd0 = make_desc_kmajor_sw128(kv_addr0);
-            const uint64_t vd0 = make_desc_mnmajor_sw128(kv_addr0, kBoxBytes);
+            const uint64_t vd0 = Cfg::FP8 ? make_desc_kmajor_sw128(kv_addr0) : make_desc_mnmajor_sw128(kv_addr0, kBoxBytes);
             auto stage_off = [](int stage) -> uint64_t {
                 return static_cast<uint64_t>(stage * (Cfg::kTileBytes >> 4));
             };
@@ -1377,6 +1444,55 @@ __global__ void __launch_bounds__(256) splitkv_combine_kernel(const CombineArgs 
     }
 }
 
+// fp8 V transpose: V [B*H][N][128] e4m3 -> V^T [B*H][128][vt_cols] (keys contiguous, zeros for
+// keys >= N), so that P.V reads V^T K-major like Q K^T reads K. One CTA per 64 keys of a head:
+// 64 rows of 128 bytes in through shared memory, 128 rows of 64 bytes out, 16-byte accesses.
+__global__ void __launch_bounds__(256) fp8_transpose_v_kernel(const uint8_t* __restrict__ v,
+                                                               uint8_t* __restrict__ vt, int n, int vt_cols) {
+    __shared__ __align__(16) uint8_t tile[64][128 + 16];
+    const long long bh = blockIdx.y;
+    const int k0 = static_cast<int>(blockIdx.x) * 64;
+    const uint8_t* src = v + bh * n * 128ll;
+    for (int i = static_cast<int>(threadIdx.x); i < 64 * 8; i += 256) {
+        const int r = i / 8;
+        const int c = i % 8;
+        uint4 val = make_uint4(0u, 0u, 0u, 0u);
+        if (k0 + r < n) {
+            val = *reinterpret_cast<const uint4*>(src + static_cast<long long>(k0 + r) * 128 + c * 16);
+        }
+        *reinterpret_cast<uint4*>(&tile[r][c * 16]) = val;
+    }
+    __syncthreads();
+    uint8_t* dst = vt + bh * 128ll * vt_cols;
+    for (int i = static_cast<int>(threadIdx.x); i < 128 * 4; i += 256) {
+        const int dd = i / 4;
+        const int g = i % 4;
+        const int kk = k0 + g * 16;
+        if (kk >= vt_cols) {
+            continue;
+        }
+        uint32_t w[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            uint32_t x = 0;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                x |= static_cast<uint32_t>(tile[g * 16 + q * 4 + b][dd]) << (8 * b);
+            }
+            w[q] = x;
+        }
+        *reinterpret_cast<uint4*>(dst + static_cast<long long>(dd) * vt_cols + kk) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+cudaError_t launch_fp8_transpose_v(const void* v, void* vt, int num_bh, int seqlen, cudaStream_t stream) {
+    const int vt_cols = (seqlen + 15) / 16 * 16;
+    const dim3 grid(static_cast<unsigned>((vt_cols + 63) / 64), static_cast<unsigned>(num_bh));
+    fp8_transpose_v_kernel<<<grid, 256, 0, stream>>>(static_cast<const uint8_t*>(v), static_cast<uint8_t*>(vt),
+                                                     seqlen, vt_cols);
+    return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------------------------------
 // Host-side dispatch
 // ------------------------------------------------------------------------------------------
@@ -1490,10 +1606,10 @@ Plan make_plan(int num_bh, int seqlen, int head_dim, bool causal, int variant, i
     return p;
 }
 
-template <int D, bool CAUSAL, int VARIANT, bool BF16 = false>
+template <int D, bool CAUSAL, int VARIANT, bool BF16 = false, bool FP8 = false>
 cudaError_t launch_cfg(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                        const CUtensorMap& tm_o, const FwdArgs& args, const Plan& plan, cudaStream_t stream) {
-    using Cfg = FwdCfg<D, CAUSAL, VARIANT, BF16>;
+    using Cfg = FwdCfg<D, CAUSAL, VARIANT, BF16, FP8>;
     auto* kernel = fa_fwd_sm100_kernel<Cfg>;
     cudaError_t err = ensure_smem_limit<fa_fwd_sm100_kernel<Cfg>>(Cfg::kSmemAlloc);
     if (err != cudaSuccess) {
@@ -1505,6 +1621,20 @@ cudaError_t launch_cfg(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const C
     kernel<<<dim3(static_cast<unsigned>(plan.ctas)), Cfg::kThreads, Cfg::kSmemAlloc, stream>>>(tm_q, tm_k, tm_v,
                                                                                               tm_o, args);
     return cudaGetLastError();
+}
+
+template <bool CAUSAL>
+cudaError_t launch_variant_fp8(int variant, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                               const CUtensorMap& tm_v, const CUtensorMap& tm_o, const FwdArgs& args,
+                               const Plan& plan, cudaStream_t stream) {
+    switch (variant) {
+        case kVariantBaseline:
+            return launch_cfg<128, CAUSAL, kVariantBaseline, false, true>(tm_q, tm_k, tm_v, tm_o, args, plan, stream);
+        case kVariantOpt:
+            return launch_cfg<128, CAUSAL, kVariantOpt, false, true>(tm_q, tm_k, tm_v, tm_o, args, plan, stream);
+        default:
+            return cudaErrorInvalidValue;
+    }
 }
 
 template <int D, bool CAUSAL>
@@ -1538,11 +1668,22 @@ cudaError_t launch_forward(const FwdProblem& prob, const FwdArgs& args, const Pl
                            cudaStream_t stream) {
     // This kernel: 128-row boxes for Q, K, V and O.
     CUtensorMap maps[4];
-    const void* ptrs[4] = {prob.q, prob.k, prob.v, prob.o};
-    for (int i = 0; i < 4; ++i) {
-        if (encode_bhnd_map(&maps[i], ptrs[i], prob.num_bh, prob.seqlen, prob.head_dim, kBM, prob.bf16) !=
-            CUDA_SUCCESS) {
+    if (prob.fp8) {
+        // e4m3 Q and K with 128-byte rows, V^T (128 keys x 128 rows per box), fp16 O.
+        if (prob.head_dim != 128 || prob.vt == nullptr ||
+            encode_u8_map(&maps[0], prob.q, 128, prob.seqlen, prob.num_bh, 128, kBM) != CUDA_SUCCESS ||
+            encode_u8_map(&maps[1], prob.k, 128, prob.seqlen, prob.num_bh, 128, kBN) != CUDA_SUCCESS ||
+            encode_u8_map(&maps[2], prob.vt, prob.vt_cols, 128, prob.num_bh, kBN, 128) != CUDA_SUCCESS ||
+            encode_bhnd_map(&maps[3], prob.o, prob.num_bh, prob.seqlen, 128, kBM, false) != CUDA_SUCCESS) {
             return cudaErrorInvalidValue;
+        }
+    } else {
+        const void* ptrs[4] = {prob.q, prob.k, prob.v, prob.o};
+        for (int i = 0; i < 4; ++i) {
+            if (encode_bhnd_map(&maps[i], ptrs[i], prob.num_bh, prob.seqlen, prob.head_dim, kBM, prob.bf16) !=
+                CUDA_SUCCESS) {
+                return cudaErrorInvalidValue;
+            }
         }
     }
     FwdArgs a = args;
@@ -1563,6 +1704,10 @@ cudaError_t launch_forward(const FwdProblem& prob, const FwdArgs& args, const Pl
     a.tail_from = plan.tail_blocks > 0 ? plan.row_blocks - plan.tail_blocks : plan.items;
     const int variant = prob.variant;
     const bool bf16 = prob.bf16;
+    if (prob.fp8) {
+        return prob.causal ? launch_variant_fp8<true>(variant, maps[0], maps[1], maps[2], maps[3], a, plan, stream)
+                           : launch_variant_fp8<false>(variant, maps[0], maps[1], maps[2], maps[3], a, plan, stream);
+    }
     if (prob.head_dim == 64) {
         return prob.causal
                    ? launch_variant<64, true>(variant, bf16, maps[0], maps[1], maps[2], maps[3], a, plan, stream)

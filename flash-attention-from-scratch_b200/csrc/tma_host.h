@@ -49,4 +49,24 @@ inline CUresult encode_bhnd_map(CUtensorMap* map, const void* base, int heads, i
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
+// 3-D map over a contiguous [dim2][dim1][dim0] tensor of bytes (e4m3 elements): box {box0,
+// box1, 1}, 128-byte swizzle (box0 = 128), zero fill out of bounds. dim0 must be a multiple of
+// 16 (the row stride is dim0 bytes).
+inline CUresult encode_u8_map(CUtensorMap* map, const void* base, int dim0, int dim1, int dim2, int box0,
+                              int box1) {
+    auto fn = tensor_map_encoder();
+    if (fn == nullptr) {
+        return CUDA_ERROR_NOT_SUPPORTED;
+    }
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(dim0), static_cast<cuuint64_t>(dim1),
+                                static_cast<cuuint64_t>(dim2)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(dim0),
+                                   static_cast<cuuint64_t>(dim1) * static_cast<cuuint64_t>(dim0)};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(box0), static_cast<cuuint32_t>(box1), 1};
+    const cuuint32_t elem_strides[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, elem_strides,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
 }  // namespace fa_sm100

@@ -32,6 +32,7 @@ VARIANTS = {"baseline": 0, "opt": 1, "fp16acc": 2}
 # FaFwdParams.dtype (FA_DTYPE_*): the element type of q, k, v and O. bfloat16 is an extension
 # of the reference, which takes float16 only (csrc/bindings.cpp:34).
 DTYPES = {torch.float16: 0, torch.bfloat16: 1}
+FA_DTYPE_FLOAT8_E4M3 = 2
 
 
 class FaFwdParams(ctypes.Structure):
@@ -110,6 +111,11 @@ def _load() -> ctypes.CDLL:
     lib.fa_plan.restype = ctypes.c_int
     lib.fa_flash_fwd_auto.argtypes = [ctypes.POINTER(FaFwdParams), ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]
     lib.fa_flash_fwd_auto.restype = ctypes.c_int
+    lib.fa_fp8_workspace_size.argtypes = [ctypes.POINTER(FaFwdParams), ctypes.POINTER(ctypes.c_uint64)]
+    lib.fa_fp8_workspace_size.restype = ctypes.c_int
+    lib.fa_flash_fwd_fp8.argtypes = [ctypes.POINTER(FaFwdParams), ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                     ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]
+    lib.fa_flash_fwd_fp8.restype = ctypes.c_int
     return lib
 
 
@@ -250,6 +256,58 @@ def forward_splitkv(
                     ws = torch.empty(int(nbytes.value), dtype=torch.uint8, device=q.device)
                     rc = lib.fa_flash_fwd_splitkv(ctypes.byref(params), splits, ctypes.c_void_p(ws.data_ptr()),
                                                   nbytes.value, ctypes.c_void_p(stream))
+            if rc != FA_OK:
+                _raise(rc)
+    return o
+
+
+def forward_fp8(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    q_descale: float,
+    k_descale: float,
+    v_descale: float,
+    causal: bool = False,
+    softmax_scale: float | None = None,
+    variant: str = "opt",
+) -> torch.Tensor:
+    """fp8 forward (not in the reference): q, k, v float8_e4m3fn [B, H, N, 128] CUDA tensors
+    holding x / descale per tensor; O = softmax(scale * (q q_descale)(k k_descale)^T)
+    (v v_descale) as float16. fa_flash_fwd_fp8 on the current stream; its transposed-V workspace
+    is a torch allocation, like O."""
+    for t in (q, k, v):
+        if not t.is_cuda:
+            raise RuntimeError("q, k, v must be CUDA tensors")
+        if t.dtype != torch.float8_e4m3fn:
+            raise RuntimeError("q, k, v must be float8_e4m3fn")
+        if not t.is_contiguous():
+            raise RuntimeError("q, k, v must be contiguous")
+        if t.dim() != 4:
+            raise RuntimeError("q, k, v must have shape [B, H, N, D]")
+    if q.shape != k.shape or q.shape != v.shape:
+        raise RuntimeError("q, k, v must have the same shape")
+    if q.device != k.device or q.device != v.device:
+        raise RuntimeError("q, k, v must be on the same device")
+    with torch.cuda.device(q.device):
+        o = torch.empty(q.shape, dtype=torch.float16, device=q.device)
+        head_dim = q.shape[3]
+        scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(head_dim)
+        if q.shape[2] > 0:
+            p = FaFwdParams()
+            p.q, p.k, p.v, p.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr()
+            p.batch, p.heads, p.seqlen, p.head_dim = (int(x) for x in q.shape)
+            p.softmax_scale = float(scale)
+            p.causal = 1 if causal else 0
+            p.variant = parse_variant(variant)
+            p.dtype = FA_DTYPE_FLOAT8_E4M3
+            nbytes = ctypes.c_uint64(0)
+            rc = lib.fa_fp8_workspace_size(ctypes.byref(p), ctypes.byref(nbytes))
+            if rc == FA_OK:
+                ws = torch.empty(max(16, int(nbytes.value)), dtype=torch.uint8, device=q.device)
+                stream = torch.cuda.current_stream(q.device).cuda_stream
+                rc = lib.fa_flash_fwd_fp8(ctypes.byref(p), float(q_descale), float(k_descale), float(v_descale),
+                                          ctypes.c_void_p(ws.data_ptr()), ws.numel(), ctypes.c_void_p(stream))
             if rc != FA_OK:
                 _raise(rc)
     return o

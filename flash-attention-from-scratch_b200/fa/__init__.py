@@ -4,6 +4,7 @@
     o = fa.forward(q, k, v, causal=False)      # q, k, v: [B, H, N, D] fp16 CUDA, D in {64, 128}
     o = fa.forward(q, k, v, fp16_accum=True)   # P.V accumulated in fp16 per key tile
     o = fa.forward(qb, kb, vb)                  # bfloat16 q, k, v (an extension): O in bf16
+    o = fa.forward_fp8(q8, k8, v8, qs, ks, vs)  # e4m3 q, k, v with descales (an extension): fp16 O
 
 Same public surface as the reference package (fa/__init__.py:14-38): ``forward``,
 ``forward_variant`` and ``attention_reference``; plus ``forward_splitkv``, ``forward_host`` (CPU
@@ -48,6 +49,33 @@ def forward_variant(
     return _C.forward(q, k, v, causal, None, variant)
 
 
+def quantize_fp8(x: torch.Tensor) -> tuple[torch.Tensor, float]:
+    """Per-tensor e4m3 quantisation for forward_fp8: (x / s rounded to float8_e4m3fn, s) with
+    s = max|x| / 448 (e4m3's largest finite value), so that x ~ x8 * s."""
+    amax = float(x.detach().abs().max()) if x.numel() > 0 else 0.0
+    s = amax / 448.0 if amax > 0.0 else 1.0
+    return (x.float() / s).to(torch.float8_e4m3fn), s
+
+
+def forward_fp8(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    q_descale: float,
+    k_descale: float,
+    v_descale: float,
+    causal: bool = False,
+    softmax_scale: float | None = None,
+    variant: str = "opt",
+) -> torch.Tensor:
+    """fp8 forward (not in the reference, which lists fp8 as not done): q, k, v are
+    float8_e4m3fn [B, H, N, 128] holding x / descale (see quantize_fp8); returns the float16
+    O = softmax(scale (q q_descale)(k k_descale)^T) (v v_descale). Scores and accumulators are
+    fp32; P enters the P.V MMA as e4m3 (scaled into e4m3's range), so the result carries fp8
+    rounding, unlike forward(). variant 'opt' (lazy threshold 2^4 here) or 'baseline'."""
+    return _C.forward_fp8(q, k, v, q_descale, k_descale, v_descale, causal, softmax_scale, variant)
+
+
 def forward_splitkv(
     q: torch.Tensor,
     k: torch.Tensor,
@@ -64,5 +92,5 @@ def forward_splitkv(
     return _C.forward_splitkv(q, k, v, causal, softmax_scale, variant, num_splits)
 
 
-__all__ = ["forward", "forward_variant", "forward_splitkv", "forward_host", "attention_reference",
-           "forward_sharded", "plan_shards"]
+__all__ = ["forward", "forward_variant", "forward_splitkv", "forward_fp8", "quantize_fp8", "forward_host",
+           "attention_reference", "forward_sharded", "plan_shards"]

@@ -52,6 +52,7 @@ typedef struct CUstream_st* fa_stream_t;
  * for the P.V MMA and fp32 accumulation; FA_VARIANT_FP16ACC needs float16. */
 #define FA_DTYPE_FLOAT16 0
 #define FA_DTYPE_BFLOAT16 1
+#define FA_DTYPE_FLOAT8_E4M3 2 /* q, k, v e4m3 and o float16: fa_flash_fwd_fp8 only */
 
 /* Forward parameters (reference fa::FlashFwdParams, csrc/flash_fwd.h:18-30).
  * q, k, v, o: [batch, heads, seqlen, head_dim] of `dtype` (float16 unless set; all four the
@@ -157,6 +158,26 @@ FA_API int fa_plan(const FaFwdParams* params, int32_t num_sms, FaPlan* plan_out)
  * work on `stream` has completed. Results are deterministic for a given device type. */
 FA_API int fa_flash_fwd_auto(const FaFwdParams* params, void* workspace, uint64_t workspace_bytes,
                              fa_stream_t stream);
+
+/* ---- fp8 (e4m3) inputs (no counterpart in the reference, which lists fp8 attention as not
+ *      done: docs/fa3_fa4_techniques.md:22,132-138). q, k, v hold e4m3 values with one descale
+ *      per tensor (the real value is the e4m3 value times its descale), o is float16; head_dim
+ *      128, the baseline or opt variant (opt's lazy threshold is 2^4 here). Scores and
+ *      accumulators are fp32; P is rounded to e4m3 as p * 2^(8 - threshold) (within e4m3's
+ *      range) for the P.V MMA and the row sums add the rounded values. Key ranges are never
+ *      split. params->dtype must be FA_DTYPE_FLOAT8_E4M3 (the other entry points reject it). */
+
+/* Bytes of device workspace fa_flash_fwd_fp8 needs: V transposed, batch * heads * head_dim *
+ * (seqlen rounded up to 16). */
+FA_API int fa_fp8_workspace_size(const FaFwdParams* params, uint64_t* bytes_out);
+
+/* O = softmax(q_descale * k_descale * softmax_scale * Q K^T) (v_descale * V), Q, K, V e4m3, O
+ * float16, enqueued on `stream`: first a transpose of V into `workspace` (at least
+ * fa_fp8_workspace_size bytes, 16-byte aligned, reusable once the call's work has completed),
+ * then the forward kernel. Descales must be positive and finite. */
+FA_API int fa_flash_fwd_fp8(const FaFwdParams* params, float q_descale, float k_descale,
+                            float v_descale, void* workspace, uint64_t workspace_bytes,
+                            fa_stream_t stream);
 
 /* fa_flash_fwd_splitkv without a caller workspace, allocating nothing (no counterpart in the
  * reference), for callers that cannot allocate device memory or hand it over (a runtime whose

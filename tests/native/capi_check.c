@@ -153,11 +153,23 @@ static int check_validation(void) {
         bad = 1;
     }
     p.variant = FA_VARIANT_OPT;
-    p.dtype = 2;
+    p.dtype = 3;
     if (fa_flash_fwd(&p, NULL) != FA_ERR_INVALID_ARGUMENT || strstr(fa_last_error(), "dtype") == NULL) {
-        fprintf(stderr, "validation: dtype 2 not rejected (%s)\n", fa_last_error());
+        fprintf(stderr, "validation: dtype 3 not rejected (%s)\n", fa_last_error());
         bad = 1;
     }
+    p.dtype = FA_DTYPE_FLOAT8_E4M3;
+    p.head_dim = 128;
+    if (fa_flash_fwd(&p, NULL) != FA_ERR_INVALID_ARGUMENT || strstr(fa_last_error(), "fa_flash_fwd_fp8") == NULL) {
+        fprintf(stderr, "validation: fp8 through fa_flash_fwd not rejected (%s)\n", fa_last_error());
+        bad = 1;
+    }
+    if (fa_flash_fwd_fp8(&p, 1.0f, 1.0f, 1.0f, NULL, 0, NULL) != FA_ERR_INVALID_ARGUMENT ||
+        strstr(fa_last_error(), "workspace") == NULL) {
+        fprintf(stderr, "validation: fp8 without workspace not rejected (%s)\n", fa_last_error());
+        bad = 1;
+    }
+    p.head_dim = 64;
     p.dtype = FA_DTYPE_BFLOAT16;
     p.variant = FA_VARIANT_FP16ACC;
     if (fa_flash_fwd(&p, NULL) != FA_ERR_INVALID_ARGUMENT || strstr(fa_last_error(), "fp16acc") == NULL) {

@@ -105,3 +105,78 @@ def gpu_reference(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: boo
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
     return out.reshape(b, h, n, d)
+
+
+# ---- fp8 (e4m3) inputs: fa.forward_fp8 ------------------------------------------------------
+# The kernel rounds P to e4m3 (3 mantissa bits) for the P.V MMA, so it is compared with two
+# references: (1) an emulation of its own algorithm in fp32 torch (128-key tiles, the running
+# max with the variant's lazy threshold, p * 2^(8 - threshold) rounded to e4m3, row sums of the
+# rounded values), which it matches up to fp32 summation order and the exponential's
+# approximation (a p within ~1e-4 of an e4m3 rounding midpoint may round the other way); and
+# (2) exact fp32 attention of the dequantized inputs, from which it differs by P's e4m3
+# rounding (up to 2^-4 relative per element).
+FP8_LAZY_THRESHOLD = {"opt": 4.0, "baseline": 0.0}
+
+
+def _exp2_poly_deg3(z: torch.Tensor) -> torch.Tensor:
+    """The kernel's software 2^x (exp2_poly2_deg3 in csrc/sm100_ptx.cuh) in fp32 torch: j =
+    round(z) through the 1.5 * 2^23 trick, f = z - j, a cubic in f, j added to the exponent bits.
+    torch rounds the multiply and the add of each step separately where the kernel fuses them:
+    the results differ by about an ulp."""
+    r23 = torch.tensor(12582912.0, dtype=torch.float32, device=z.device)
+    z = torch.clamp(z, min=-126.0)
+    t = z + r23
+    f = z - (t - r23)
+    p = (0.05500892922282219 * f + 0.24221095442771912) * f
+    p = (p + 0.6932829022407532) * f + 1.0
+    bits = (p.view(torch.int32).to(torch.int64) + ((t.view(torch.int32).to(torch.int64) & 0x1FF) << 23)) & 0xFFFFFFFF
+    bits = torch.where(bits >= 2**31, bits - 2**32, bits).to(torch.int32)
+    return bits.view(torch.float32)
+
+
+def _kernel_exp2(z: torch.Tensor, cols: int) -> torch.Tensor:
+    """2^z as the d = 128 kernel computes it per key column: the polynomial on the columns c of
+    a tile with c mod 16 < 2 (one pair in eight), the exponential unit (about correctly rounded)
+    elsewhere."""
+    poly = (torch.arange(cols, device=z.device) % 16) < 2
+    return torch.where(poly, _exp2_poly_deg3(z), torch.exp2(z))
+
+
+@torch.no_grad()
+def fp8_emulated_reference(q8, k8, v8, qs, ks, vs, causal, variant="opt", softmax_scale=None, tile=128):
+    """fa.forward_fp8's algorithm in fp32 torch on q8's device: [B, H, N, d] e4m3 in, fp32 out."""
+    import math
+
+    b, h, n, d = q8.shape
+    q, k, v = (t.float().reshape(b * h, n, d) for t in (q8, k8, v8))
+    scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(d)
+    s_log2 = torch.tensor(float(scale) * float(qs) * float(ks) * math.log2(math.e), dtype=torch.float32).item()
+    thr = FP8_LAZY_THRESHOLD[variant]
+    shift = 8.0 - thr
+    rows = torch.arange(n, device=q.device)
+    m = torch.full((b * h, n), -math.inf, device=q.device)
+    l = torch.zeros((b * h, n), device=q.device)
+    o = torch.zeros((b * h, n, d), device=q.device)
+    for k0 in range(0, n, tile):
+        kt, vt = k[:, k0:k0 + tile], v[:, k0:k0 + tile]
+        x = (q @ kt.transpose(1, 2)) * s_log2
+        keys = torch.arange(k0, k0 + kt.shape[1], device=q.device)
+        if causal:
+            x = x.masked_fill(keys[None, None, :] > rows[None, :, None], -math.inf)
+        tmax = x.max(dim=-1).values
+        new_m = torch.where(tmax > m + thr, tmax, m)
+        used = torch.where(new_m == -math.inf, torch.zeros_like(new_m), new_m)
+        alpha = torch.where(m == -math.inf, torch.zeros_like(m), torch.exp2(m - used))
+        z = x + (shift - used)[..., None]
+        p = _kernel_exp2(z, kt.shape[1]).to(torch.float8_e4m3fn).float()
+        l = l * alpha + p.sum(dim=-1)
+        o = o * alpha[..., None] + p @ vt
+        m = new_m
+    out = o / l[..., None] * float(vs)
+    return out.reshape(b, h, n, d)
+
+
+@torch.no_grad()
+def fp8_exact_reference(q8, k8, v8, qs, ks, vs, causal, budget_bytes: int = 4 << 30):
+    """Exact fp32 attention (fa.attention_reference) of the dequantized inputs."""
+    return gpu_reference((q8.float() * qs), (k8.float() * ks), (v8.float() * vs), causal, budget_bytes)

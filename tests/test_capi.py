@@ -76,7 +76,9 @@ def _params(**kw):
         (dict(batch=300, heads=300), "65535"),
         (dict(q=0x10002), "16-byte aligned"),
         (dict(variant=7), "unknown variant"),
-        (dict(dtype=2), "dtype must be FA_DTYPE_FLOAT16 or FA_DTYPE_BFLOAT16"),
+        (dict(dtype=3), "dtype must be FA_DTYPE_FLOAT16, FA_DTYPE_BFLOAT16 or FA_DTYPE_FLOAT8_E4M3"),
+        (dict(dtype=2), "float8 inputs need head_dim 128"),
+        (dict(dtype=2, head_dim=128), "float8 inputs go through fa_flash_fwd_fp8"),
         (dict(dtype=1, variant=2), "fp16acc variant needs float16 inputs"),
     ],
 )
@@ -153,3 +155,20 @@ def test_splitkv_validation(splits, ws, nbytes, msg):
     rc = _C.lib.fa_flash_fwd_splitkv(ctypes.byref(p), splits, ctypes.c_void_p(ws), nbytes, None)
     assert rc == _C.FA_ERR_INVALID_ARGUMENT
     assert msg in _C.lib.fa_last_error().decode()
+
+
+def test_fp8_entry_validates_before_any_cuda_call():
+    p = _params(dtype=2, head_dim=128, batch=2, heads=3, seqlen=1000)
+    out = ctypes.c_uint64(0)
+    assert _C.lib.fa_fp8_workspace_size(ctypes.byref(p), ctypes.byref(out)) == _C.FA_OK
+    assert out.value == 2 * 3 * 128 * 1008  # seqlen rounded up to 16
+    ws, n = 0x50000, out.value
+    call = lambda prm, qd, kd, vd, w, nb: _C.lib.fa_flash_fwd_fp8(ctypes.byref(prm), qd, kd, vd, w, nb, None)
+    assert call(p, 0.0, 1.0, 1.0, ws, n) == _C.FA_ERR_INVALID_ARGUMENT
+    assert "descales must be positive" in _C.lib.fa_last_error().decode()
+    assert call(p, 1.0, float("inf"), 1.0, ws, n) == _C.FA_ERR_INVALID_ARGUMENT
+    assert call(p, 1.0, 1.0, 1.0, ws, n - 1) == _C.FA_ERR_INVALID_ARGUMENT
+    assert "workspace must be 16-byte aligned" in _C.lib.fa_last_error().decode()
+    assert call(p, 1.0, 1.0, 1.0, ws + 8, n) == _C.FA_ERR_INVALID_ARGUMENT
+    assert call(_params(head_dim=128), 1.0, 1.0, 1.0, ws, n) == _C.FA_ERR_INVALID_ARGUMENT
+    assert "must be FA_DTYPE_FLOAT8_E4M3" in _C.lib.fa_last_error().decode()

@@ -30,3 +30,28 @@ def test_literal_bound_met_reports_nothing():
         warnings.simplefilter("always")
         check_tolerance(out, ref, "opt", "clean case")
     assert not any(issubclass(w.category, LiteralBoundMiss) for w in rec)
+
+
+def test_fp8_emulation_tracks_exact_attention():
+    """The fp8 emulated reference (tests/parity.py) against exact attention of the same e4m3
+    values: differences are P's e4m3 rounding only (relative RMS a few percent), and with every
+    p exactly representable (q = 0: all p = 2^(8 - threshold)) it is exact up to fp32."""
+    import torch
+
+    import fa
+    from fa.reference import attention_reference
+    from parity import fp8_emulated_reference
+
+    g = torch.Generator().manual_seed(3)
+    q, k, v = (torch.randn(1, 2, 300, 128, generator=g) for _ in range(3))
+    (q8, qs), (k8, ks), (v8, vs) = fa.quantize_fp8(q), fa.quantize_fp8(k), fa.quantize_fp8(v)
+    for causal in (False, True):
+        for variant in ("opt", "baseline"):
+            em = fp8_emulated_reference(q8, k8, v8, qs, ks, vs, causal, variant)
+            ex = attention_reference(q8.float() * qs, k8.float() * ks, v8.float() * vs, causal)
+            rms = float(((em - ex) ** 2).mean().sqrt() / (ex**2).mean().sqrt())
+            assert rms < 5e-2, (causal, variant, rms)
+    zq = torch.zeros_like(q8)
+    em = fp8_emulated_reference(zq, k8, v8, 1.0, ks, vs, False)
+    ex = (v8.float() * vs).mean(dim=2, keepdim=True).expand_as(em)
+    assert float((em - ex).abs().max()) < 1e-5
