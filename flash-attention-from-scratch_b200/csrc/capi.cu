@@ -113,6 +113,9 @@ int validate(const FaFwdParams* p) {
 }
 
 fa_sm100::Plan plan_for(const FaFwdParams* p, int num_splits, int sm_count) {
+    if (p->dtype == FA_DTYPE_FLOAT8_E4M3) {
+        num_splits = 1;  // fa_flash_fwd_fp8 never splits key ranges
+    }
     return fa_sm100::make_plan(p->batch * p->heads, p->seqlen, p->head_dim, p->causal != 0, p->variant,
                                num_splits, num_splits == 0, sm_count);
 }

@@ -29,7 +29,7 @@ int validate(const FaFwdParams* p);
 
 // The schedule for `p` on a GPU with sm_count SMs: num_splits key ranges per row block, or,
 // with num_splits == 0, the library's choice (split-KV for few row blocks, a tail split of the
-// last partial wave).
+// last partial wave). e4m3 problems always get one key range.
 fa_sm100::Plan plan_for(const FaFwdParams* p, int num_splits, int sm_count);
 
 // fp8 launch extras: per-tensor descales and the transposed-V workspace.

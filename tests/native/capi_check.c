@@ -18,6 +18,10 @@
  * bf16 cases (FaFwdParams.dtype = FA_DTYPE_BFLOAT16) draw bf16 values that fp16 also holds
  * exactly (magnitudes below 2^-14 set to 0), so the same oracle checks them; their bounds are
  * the fp16 ones times 8, the ratio of the two formats' unit roundoffs.
+ * fp8 cases (fa_flash_fwd_fp8) quantise each tensor to e4m3 with a power-of-two descale, so the
+ * dequantized values are exact in fp16 and the oracle sees exactly what the kernel multiplies;
+ * the check is the fp8 contract against exact attention: relative RMS error <= 5e-2 and
+ * mean-abs <= 1e-2 (P is rounded to e4m3 for the P.V MMA).
  */
 #include <cuda_runtime.h>
 #include <math.h>
@@ -112,6 +116,143 @@ static double bf16_bits_to_double(uint16_t b) {
 }
 
 static double round_to_bf16(double x) { return bf16_bits_to_double(float_to_bf16_bits((float)x)); }
+
+static const char* variant_name(int v);
+
+/* binary64 -> e4m3 (bias 7, no infinities, largest finite 448), round to nearest even,
+ * saturating; the value is finite. */
+static uint8_t double_to_e4m3(double x) {
+    const uint8_t sign = x < 0 ? 0x80u : 0u;
+    const double a = fabs(x);
+    if (a < ldexp(1.0, -6)) { /* subnormal: m * 2^-9 */
+        return sign | (uint8_t)nearbyint(a * 512.0); /* m = 8 encodes 2^-6, the smallest normal */
+    }
+    int ex = 0;
+    const double fr = frexp(a, &ex); /* a = fr * 2^ex, fr in [0.5, 1) */
+    int e = ex - 1;
+    int q = (int)nearbyint((fr * 2.0 - 1.0) * 8.0);
+    if (q == 8) {
+        q = 0;
+        ++e;
+    }
+    int code = ((e + 7) << 3) | q;
+    if (code > 0x7e) {
+        code = 0x7e;
+    }
+    return sign | (uint8_t)code;
+}
+
+static double e4m3_to_double(uint8_t c) {
+    const int e = (c >> 3) & 0xf, m = c & 7;
+    const double v = e == 0 ? ldexp((double)m, -9) : ldexp(1.0 + m / 8.0, e - 7);
+    return (c & 0x80u) ? -v : v;
+}
+
+/* One fp8 case through fa_flash_fwd_fp8 against the double-precision oracle. */
+static int run_fp8_case(int b, int h, int n, int causal, int variant, uint64_t seed) {
+    const int d = 128;
+    const size_t elems = (size_t)b * h * n * d;
+    uint8_t* q8[3];
+    uint16_t* deq[3]; /* the dequantized values as fp16 bits (exact): the oracle's inputs */
+    float descale[3];
+    rng_state = seed * 0x9E3779B97F4A7C15ULL + 1;
+    for (int t = 0; t < 3; ++t) {
+        double* x = (double*)malloc(elems * sizeof(double));
+        double amax = 0.0;
+        for (size_t i = 0; i < elems; ++i) {
+            x[i] = rng_normal();
+            amax = fabs(x[i]) > amax ? fabs(x[i]) : amax;
+        }
+        const double s = ldexp(1.0, (int)ceil(log2(amax / 448.0))); /* power of two */
+        descale[t] = (float)s;
+        q8[t] = (uint8_t*)malloc(elems);
+        deq[t] = (uint16_t*)malloc(elems * 2);
+        for (size_t i = 0; i < elems; ++i) {
+            q8[t][i] = double_to_e4m3(x[i] / s);
+            deq[t][i] = float_to_half_bits((float)(e4m3_to_double(q8[t][i]) * s));
+        }
+        free(x);
+    }
+    void *dq, *dk, *dv, *dout, *ws;
+    CHECK_CUDA(cudaMalloc(&dq, elems));
+    CHECK_CUDA(cudaMalloc(&dk, elems));
+    CHECK_CUDA(cudaMalloc(&dv, elems));
+    CHECK_CUDA(cudaMalloc(&dout, elems * 2));
+    CHECK_CUDA(cudaMemcpy(dq, q8[0], elems, cudaMemcpyHostToDevice));
+    CHECK_CUDA(cudaMemcpy(dk, q8[1], elems, cudaMemcpyHostToDevice));
+    CHECK_CUDA(cudaMemcpy(dv, q8[2], elems, cudaMemcpyHostToDevice));
+    FaFwdParams p;
+    memset(&p, 0, sizeof(p));
+    p.q = dq;
+    p.k = dk;
+    p.v = dv;
+    p.o = dout;
+    p.batch = b;
+    p.heads = h;
+    p.seqlen = n;
+    p.head_dim = d;
+    p.softmax_scale = (float)(1.0 / sqrt((double)d));
+    p.causal = (uint8_t)causal;
+    p.variant = (uint8_t)variant;
+    p.dtype = FA_DTYPE_FLOAT8_E4M3;
+    uint64_t ws_bytes = 0;
+    if (fa_fp8_workspace_size(&p, &ws_bytes) != FA_OK) {
+        fprintf(stderr, "fa_fp8_workspace_size: %s\n", fa_last_error());
+        exit(1);
+    }
+    CHECK_CUDA(cudaMalloc(&ws, ws_bytes));
+    cudaStream_t stream;
+    CHECK_CUDA(cudaStreamCreate(&stream));
+    uint16_t* out = (uint16_t*)malloc(elems * 2);
+    uint16_t* out2 = (uint16_t*)malloc(elems * 2);
+    int failed = 0;
+    for (int rep = 0; rep < 2; ++rep) {
+        const int rc = fa_flash_fwd_fp8(&p, descale[0], descale[1], descale[2], ws, ws_bytes, (fa_stream_t)stream);
+        if (rc != FA_OK) {
+            fprintf(stderr, "fa_flash_fwd_fp8 returned %d: %s\n", rc, fa_last_error());
+            exit(1);
+        }
+        CHECK_CUDA(cudaStreamSynchronize(stream));
+        CHECK_CUDA(cudaMemcpy(rep == 0 ? out : out2, dout, elems * 2, cudaMemcpyDeviceToHost));
+    }
+    if (memcmp(out, out2, elems * 2) != 0) {
+        fprintf(stderr, "fp8 repeat launch differs\n");
+        failed = 1;
+    }
+    double* ref = (double*)malloc(elems * sizeof(double));
+    if (ref == NULL || oracle_attention_f64(deq[0], deq[1], deq[2], (int64_t)b * h, n, d, causal,
+                                            (double)p.softmax_scale, ref) != 0) {
+        fprintf(stderr, "oracle: out of memory\n");
+        exit(2);
+    }
+    double se = 0.0, sr = 0.0, sum_abs = 0.0;
+    for (size_t i = 0; i < elems; ++i) {
+        const double e = half_bits_to_double(out[i]) - ref[i];
+        se += e * e;
+        sr += ref[i] * ref[i];
+        sum_abs += fabs(e);
+    }
+    const double rel_rms = sqrt(se / (sr > 0.0 ? sr : 1.0)), mean_abs = sum_abs / (double)elems;
+    if (!(rel_rms <= 5e-2) || !(mean_abs <= 1e-2)) {
+        failed = 1;
+    }
+    printf("B%d H%d N%d D%d %s %-8s fp8  rel-rms %.3e (bound 5e-2) mean-abs %.3e (bound 1e-2) %s\n", b, h, n, d,
+           causal ? "causal" : "full  ", variant_name(variant), rel_rms, mean_abs, failed ? "FAILED" : "ok");
+    free(ref);
+    free(out);
+    free(out2);
+    for (int t = 0; t < 3; ++t) {
+        free(q8[t]);
+        free(deq[t]);
+    }
+    cudaFree(dq);
+    cudaFree(dk);
+    cudaFree(dv);
+    cudaFree(dout);
+    cudaFree(ws);
+    cudaStreamDestroy(stream);
+    return failed;
+}
 
 static const char* variant_name(int v) {
     return v == FA_VARIANT_BASELINE ? "baseline" : v == FA_VARIANT_OPT ? "opt" : "fp16acc";
@@ -337,6 +478,8 @@ int main(int argc, char** argv) {
             const int* c = cases[i];
             failed |= run_case(c[0], c[1], c[2], c[3], c[4], c[5], c[6], 0, 1234 + i);
         }
+        failed |= run_fp8_case(1, 2, 700, 1, FA_VARIANT_OPT, 77);
+        failed |= run_fp8_case(2, 1, 385, 0, FA_VARIANT_BASELINE, 78);
     } else {
         fprintf(stderr, "usage: %s [B H N D CAUSAL VARIANT ITERS [bf16]]\n", argv[0]);
         return 2;

@@ -29,8 +29,9 @@ def test_native_driver_validates_without_gpu():
 
 @pytest.mark.gpu
 def test_native_driver_cases_match_oracle():
-    """Nine shapes x variants x element types (two bf16 cases) through fa_flash_fwd from C, each
-    against the double-precision oracle, a bitwise repeat and the watchdog word."""
+    """Nine shapes x variants x element types (two bf16 cases) through fa_flash_fwd and two e4m3
+    cases through fa_flash_fwd_fp8 from C, each against the double-precision oracle, a bitwise
+    repeat and the watchdog word."""
     res = _run()
     print(res.stdout)
     assert res.returncode == 0, res.stdout + res.stderr
