@@ -157,3 +157,13 @@ def test_bf16_cfg3_sampled_heads(causal):
         sl = (slice(b, b + 1), slice(h, h + 1))
         ref = gpu_reference(qd[sl], kd[sl], vd[sl], causal)
         check_tolerance_bf16(out[sl].float(), ref, f"bf16 cfg3 head ({b},{h}) causal={causal}")
+
+
+def test_bf16_forward_host_matches_device_call():
+    """Host buffers in and out (fa.forward_host, copies pipelined over head chunks) give the
+    device call's bits."""
+    q, k, v, qd, kd, vd = _qkv(2, 5, 1000, 128, seed=13)
+    want = fa.forward(qd, kd, vd, causal=True).cpu()
+    got = fa.forward_host(q.pin_memory(), k.pin_memory(), v.pin_memory(), causal=True)
+    torch.cuda.synchronize()
+    assert got.dtype == BF and torch.equal(got, want)
