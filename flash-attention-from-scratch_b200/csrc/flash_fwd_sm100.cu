@@ -91,6 +91,12 @@
 #ifndef FA_MMA_ISSUERS_ACC16
 #define FA_MMA_ISSUERS_ACC16 1
 #endif
+// TMEM columns per tcgen05.ld of the softmax's S readout (32, 64 or 128): one 128-column load
+// per tile measured +1% at d = 64 (fewer instructions through the sub-partition's MIO queue,
+// which the MMA issuers share), neutral at d = 128.
+#ifndef FA_S_LD_COLS
+#define FA_S_LD_COLS 128
+#endif
 #ifndef FA_STAGES_D64
 #define FA_STAGES_D64 8  // K/V ring slots at d = 64 (16 KB each)
 #endif
@@ -525,9 +531,17 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                 }
                 tc_fence_after();
                 uint32_t sr[NC];
+                if constexpr (FA_S_LD_COLS == 128) {
+                    tmem_ld128(t_s + s_off, sr);
+                } else {
 #pragma unroll
-                for (int c = 0; c < NC / 32; ++c) {
-                    tmem_ld32(t_s + s_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+                    for (int c = 0; c < NC / FA_S_LD_COLS; ++c) {
+                        if constexpr (FA_S_LD_COLS == 64) {
+                            tmem_ld64(t_s + s_off + c * 64, *reinterpret_cast<uint32_t(*)[64]>(&sr[c * 64]));
+                        } else {
+                            tmem_ld32(t_s + s_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+                        }
+                    }
                 }
                 tmem_wait_ld();
                 if constexpr (Cfg::SEP_P) {
