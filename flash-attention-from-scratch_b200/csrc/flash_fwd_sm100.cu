@@ -64,6 +64,9 @@
 #ifndef FA_EMU_PER8_D64
 #define FA_EMU_PER8_D64 2
 #endif
+#ifndef FA_EMU_PER8_FP8
+#define FA_EMU_PER8_FP8 1  // e4m3 inputs (d = 128)
+#endif
 #ifndef FA_EMU_PER8_ACC16_D64
 #define FA_EMU_PER8_ACC16_D64 1  // fp16acc at d = 64 (its fold adds FMA-pipe work): 1/8 measured fastest
 #endif
@@ -154,7 +157,8 @@ struct FwdCfg {
     static constexpr int NQ = (ACC16 && D == 128) ? 1 : 2;
     static constexpr int kSBufs = (ACC16 && NQ == 1) ? 2 : 1;
     static constexpr bool SEP_P = !ACC16 && D == 64;
-    static constexpr int kEmuPer8 = (D == 128) ? FA_EMU_PER8_D128 : (ACC16 ? FA_EMU_PER8_ACC16_D64 : FA_EMU_PER8_D64);
+    static constexpr int kEmuPer8 =
+        FP8 ? FA_EMU_PER8_FP8 : ((D == 128) ? FA_EMU_PER8_D128 : (ACC16 ? FA_EMU_PER8_ACC16_D64 : FA_EMU_PER8_D64));
     static constexpr int kPolyDeg = (D == 128) ? FA_EXP_POLY_DEG_D128 : FA_EXP_POLY_DEG_D64;
     static constexpr int kElemBytes = FP8 ? 1 : 2;
     static constexpr int kTileBytes = kBM * D * kElemBytes;  // one Q, K or V tile (BM == BN)
