@@ -10,6 +10,11 @@
 // on diagonal / ragged tiles, lazy rescaling for the "opt" variant, per-tile fp16 partials for
 // "fp16acc") is the reference's, the machine mapping is new:
 //
+// Element types (FwdCfg's BF16 / FP8 flags, extensions of the reference): bf16 runs the same
+// pipeline with bf16 operands; e4m3 (d = 128) reads Q and K as 128-byte rows, V transposed (a
+// separate kernel writes V^T so that both MMAs read K-major operands), issues kind::f8f6f4 MMAs
+// of K = 32 and stores P as e4m3, with fp32 scores and accumulators and a float16 O.
+//
 // Work item = one (b,h) head x NQ consecutive 128-row query tiles (NQ = 2; 1 for fp16acc, d = 128)
 // x one key range (split-KV). Each CTA runs one item, or, for short rows (N <= 2048), a
 // persistent grid of one CTA per SM walks the items: every role loops over the same items
@@ -35,8 +40,9 @@
 //   S_t  columns [128 t, 128 t + 128)   scores of tile t, fp32 (fp16acc at d = 128, NQ = 1: two
 //        S buffers, columns [0, 128) and [128, 256), for alternate key tiles)
 //   O_t  columns [128 NQ kSBufs + D t, +D)  fp32 output accumulator of tile t
-//   P_t  (d = 128) columns [128 t, +64) over S_t once S_t has been read: S_t(j+1) is issued
-//        after PV_t(j), and tcgen05.mma operations of one thread execute in issue order;
+//   P_t  (d = 128) columns [128 t, +64) over S_t once S_t has been read (e4m3 inputs: four P
+//        values per column, [128 t, +32)): S_t(j+1) is issued after PV_t(j), and tcgen05.mma
+//        operations of one thread execute in issue order;
 //        (d = 64) its own columns [128 NQ + D NQ + 64 t, +64), so that S_t(j+1) can run while
 //        the softmax of tile j is still computing P_t(j).
 //   T_t  (fp16acc) the D columns after the O_t: fp16 partial of P.V over the current K/V tile,
