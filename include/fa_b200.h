@@ -173,8 +173,9 @@ FA_API int fa_fp8_workspace_size(const FaFwdParams* params, uint64_t* bytes_out)
 
 /* O = softmax(q_descale * k_descale * softmax_scale * Q K^T) (v_descale * V), Q, K, V e4m3, O
  * float16, enqueued on `stream`: first a transpose of V into `workspace` (at least
- * fa_fp8_workspace_size bytes, 16-byte aligned, reusable once the call's work has completed),
- * then the forward kernel. Descales must be positive and finite. */
+ * fa_fp8_workspace_size bytes, 16-byte aligned, overlapping none of q, k, v and o, reusable
+ * once the call's work has completed), then the forward kernel. Descales must be positive and
+ * finite. */
 FA_API int fa_flash_fwd_fp8(const FaFwdParams* params, float q_descale, float k_descale,
                             float v_descale, void* workspace, uint64_t workspace_bytes,
                             fa_stream_t stream);
